@@ -1,0 +1,484 @@
+"""Benchmark of the GDN hot path (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode_b64|decode_b1024|prefill_varlen16|prefill_8x32768]
+
+Headline (``value``): GDN decode state GB/s on configs[1] (B = 64 sequences,
+16 q/k heads, 32 v heads, d = 128, fp32 k-last state) per GPU; with N GPUs
+each rank owns its own 64 sequences and states (weak scaling, no collective),
+``value`` = algorithmic bytes of all ranks / max-over-ranks time.  A step is
+one decode call over the batch; inputs are resident in HBM and rotate over
+several buffer sets whose footprint exceeds 3x L2 (126 MB), so no step reads
+L2-resident state.  ``e2e`` times the public ``run()`` with host (pinned)
+inputs and outputs, copies included.  ``prefill`` reports configs[3] (varlen,
+16 sequences) tokens/s on the same ranks.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+C restatement in ``oracle/``, all host threads) on a bounded sample of the
+same workload and prints the same line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from __graft_entry__ import load_package  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+# ----------------------------------------------------------------------------- helpers
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", 0)), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of the
+    kernel as recorded from an ncu capture in ``profiles/<name>.txt``."""
+    p = ROOT / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].split()[0])
+    return None
+
+
+class ClockSampler:
+    """Samples SM clocks and clock-event reasons with NVML during the timed region."""
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.period = [], 0, period_s
+        self._stop = threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report no clocks
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._nv is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml_unavailable"]}
+        reasons = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world} (launch N>1 with torchrun)")
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- workloads
+def decode_sets(gdn, batch, n_sets, seed, device):
+    sets = []
+    for i in range(n_sets):
+        inp = gdn.workloads.decode_inputs(batch, seed=seed + 1000 * i, device=device)
+        inp["output"] = torch.empty(batch, 1, 32, 128, dtype=torch.bfloat16, device=device)
+        inp["new_state"] = torch.empty_like(inp["state"])
+        sets.append(inp)
+    return sets
+
+
+def decode_call(gdn, s):
+    gdn.kernel_decode.run_dps(s["q"], s["k"], s["v"], s["state"], s["A_log"], s["a"], s["dt_bias"],
+                              s["b"], s["scale"], s["output"], s["new_state"])
+
+
+def prefill_sets(gdn, seqlens, n_sets, seed, device, zero_state=False):
+    sets = []
+    for i in range(n_sets):
+        inp = gdn.workloads.prefill_inputs(seqlens, seed=seed + 1000 * i, device=device,
+                                           zero_state=zero_state)
+        T = sum(seqlens)
+        inp["output"] = torch.empty(T, 32, 128, dtype=torch.bfloat16, device=device)
+        inp["new_state"] = torch.empty_like(inp["state"])
+        if zero_state:
+            inp["state"] = None
+        sets.append(inp)
+    return sets
+
+
+def prefill_call(gdn, s):
+    gdn.kernel_prefill.run_dps(s["q"], s["k"], s["v"], s["state"], s["A_log"], s["a"], s["dt_bias"],
+                               s["b"], s["cu_seqlens"], s["scale"], s["output"], s["new_state"])
+
+
+def set_bytes(s):
+    return sum(v.numel() * v.element_size() for v in s.values() if torch.is_tensor(v))
+
+
+def time_steps(call, sets, steps, warmup, world, sampler=None):
+    """Warm up, then time exactly ``steps`` calls bracketed by barrier +
+    synchronize; per-launch CUDA events on the launching stream give the
+    kernel's average duration.  Returns (ms_per_step max over ranks, avg launch ms)."""
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        call(sets[i % len(sets)])
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    ctx = sampler if sampler is not None else _Null()
+    with ctx:
+        t0.record(stream)
+        for i in range(steps):
+            starts[i].record(stream)
+            call(sets[i % len(sets)])
+            ends[i].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    total_ms = t0.elapsed_time(t1)
+    launch_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+    return max_over_ranks(total_ms, world) / steps, launch_ms
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+# ----------------------------------------------------------------------------- e2e
+def decode_e2e(gdn, batch, steps, warmup, world, seed):
+    """Public API with host buffers: pinned host inputs -> device, run(), outputs -> pinned host."""
+    host = gdn.workloads.decode_inputs(batch, seed=seed)
+    pinned = {k: (v.pin_memory() if torch.is_tensor(v) else v) for k, v in host.items()}
+    out_h = torch.empty(batch, 1, 32, 128, dtype=torch.bfloat16).pin_memory()
+    st_h = torch.empty(batch, 32, 128, 128, dtype=torch.float32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values() if torch.is_tensor(v))
+    d2h = out_h.numel() * 2 + st_h.numel() * 4
+
+    def step():
+        d = {k: (v.to("cuda", non_blocking=True) if torch.is_tensor(v) else v) for k, v in pinned.items()}
+        o, ns = gdn.kernel_decode.run(**d)
+        out_h.copy_(o, non_blocking=True)
+        st_h.copy_(ns, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(t0.elapsed_time(t1), world) / steps, h2d, d2h
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_decode_rate(gdn, batch, budget_s, nthreads=None):
+    """C restatement of the reference recurrence on the host cores; returns
+    (GB/s, sample description, cores)."""
+    import numpy as np
+
+    from oracle import c_oracle
+
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    inp = gdn.workloads.decode_inputs(batch, seed=0)
+    args = (bits(inp["q"]), bits(inp["k"]), bits(inp["v"]), inp["state"].numpy(), inp["A_log"].numpy(),
+            bits(inp["a"]), inp["dt_bias"].numpy(), bits(inp["b"]), inp["scale"])
+    cores = nthreads or c_oracle.default_threads()
+    c_oracle.decode(*args, nthreads=cores)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        c_oracle.decode(*args, nthreads=cores)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    gb = gdn.workloads.decode_bytes_per_seq() * batch * reps / 1e9
+    return gb / el, f"{reps} full decode steps of B={batch} (16/32 heads) in {el:.1f} s", cores
+
+
+def cpu_prefill_rate(gdn, seqlens, budget_s, nthreads=None):
+    """Tokens/s of the C restatement on a sample: the first tokens of every sequence
+    (time-bounded by doubling the per-sequence prefix until the budget is used)."""
+    import numpy as np
+
+    from oracle import c_oracle
+
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    cores = nthreads or c_oracle.default_threads()
+    prefix, best = 16, None
+    while True:
+        lens = [min(prefix, L) for L in seqlens]
+        inp = gdn.workloads.prefill_inputs(lens, seed=0)
+        args = (bits(inp["q"]), bits(inp["k"]), bits(inp["v"]), inp["state"].numpy(),
+                inp["A_log"].numpy(), bits(inp["a"]), inp["dt_bias"].numpy(), bits(inp["b"]),
+                inp["cu_seqlens"].numpy(), inp["scale"])
+        t0 = time.perf_counter()
+        c_oracle.prefill(*args, nthreads=cores)
+        el = time.perf_counter() - t0
+        best = (sum(lens) / el, f"first {prefix} tokens of each of {len(lens)} sequences "
+                                f"({sum(lens)} tokens) in {el:.1f} s", cores)
+        if el * 2.5 > budget_s or prefix >= max(seqlens):
+            return best
+        prefix *= 2
+
+
+# ----------------------------------------------------------------------------- main
+def run_reference(args, world, rank):
+    """Reference arm: the reference algorithm's CPU implementation (the C
+    restatement, all host threads), same metric.  Each step is a bounded sample
+    of the workload: ``m`` of its sequences, with ``m`` sized so the whole
+    ``--steps/--warmup`` run takes about a minute."""
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import c_oracle
+
+    gdn = load_package()
+    batch = 64 if args.workload == "decode_b64" else 1024
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    inp = gdn.workloads.decode_inputs(batch, seed=0)
+    cores = c_oracle.default_threads()
+
+    def args_for(m):
+        return (bits(inp["q"][:m]), bits(inp["k"][:m]), bits(inp["v"][:m]), inp["state"][:m].numpy(),
+                inp["A_log"].numpy(), bits(inp["a"][:m]), inp["dt_bias"].numpy(), bits(inp["b"][:m]),
+                inp["scale"])
+
+    probe = args_for(min(batch, cores))
+    c_oracle.decode(*probe, nthreads=cores)
+    t0 = time.perf_counter()
+    c_oracle.decode(*probe, nthreads=cores)
+    per_seq = (time.perf_counter() - t0) / min(batch, cores)
+    per_step_budget = 60.0 / max(1, args.steps + args.warmup)
+    m = max(1, min(batch, int(per_step_budget / max(per_seq, 1e-9))))
+    sample = args_for(m)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        c_oracle.decode(*sample, nthreads=cores)
+        el = time.perf_counter() - t0
+        if i >= args.warmup:
+            vals.append(gdn.workloads.decode_bytes_per_seq() * m / el / 1e9)
+    value = statistics.median(vals)
+    bytes_step = gdn.workloads.decode_bytes_per_seq() * batch
+    line = {
+        "impl": "reference", "metric": "GDN decode state GB/s", "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": bytes_step / (value * 1e9) * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": args.workload, "batch_per_rank": batch, "num_qk_heads": 16,
+                   "num_v_heads": 32, "head_dim": 128, "state": "fp32 k-last"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"each step: {m} of the {batch} sequences (all 32 heads); median over "
+                                   f"{args.steps} steps; C restatement of the reference recurrence"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    gdn = load_package()
+    hbm_peak, bf16_peak, bf16_sust, peak_kind = measured_peaks()
+    wl = args.workload
+    result = {}
+    if wl.startswith("decode"):
+        batch = 64 if wl == "decode_b64" else 1024 // world
+        one = decode_sets(gdn, batch, 1, seed=rank, device="cuda")
+        n_sets = max(2, math.ceil(3 * L2_BYTES / set_bytes(one[0])))
+        sets = one + decode_sets(gdn, batch, n_sets - 1, seed=rank + 1, device="cuda")
+        sampler = ClockSampler(local)
+        ms, launch_ms = time_steps(lambda s: decode_call(gdn, s), sets, args.steps, args.warmup, world, sampler)
+        bytes_rank = gdn.workloads.decode_bytes_per_seq() * batch
+        total_bytes = sum_over_ranks(bytes_rank, world)
+        value = total_bytes / (ms * 1e-3) / 1e9
+        achieved = bytes_rank / (launch_ms * 1e-3) / 1e9
+        e2e_steps = max(3, min(20, args.steps // 50))
+        e2e_ms, h2d, d2h = decode_e2e(gdn, batch, e2e_steps, 2, world, seed=rank)
+        result.update(
+            metric="GDN decode state GB/s", value=value, unit="GB/s", ms_per_step=ms, dtype="f32",
+            config={"workload": wl, "batch_per_rank": batch, "num_qk_heads": 16, "num_v_heads": 32,
+                    "head_dim": 128, "state": "fp32 k-last", "rotating_buffer_sets": len(sets),
+                    "l2": f"inputs larger than L2: {len(sets)} rotating sets, "
+                          f"{len(sets) * set_bytes(sets[0]) / 1e6:.0f} MB footprint",
+                    "parallelism": f"dp{world} (sequences sharded, no collective)"},
+            roofline={"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                      "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)",
+                      "traffic": profile_traffic("gdn_decode_b64"),
+                      "kernel": "decode_kernel", "avg_launch_us": launch_ms * 1e3,
+                      "algorithmic_bytes_per_launch": bytes_rank},
+            e2e={"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                 "path": "kernel_decode.run() with pinned host inputs/outputs (state in and out)"},
+            gpu_launches=args.steps,
+            clocks=sampler.summary())
+        del sets
+    if args.prefill and not wl.startswith("prefill"):
+        wl_p = "prefill_varlen16"
+    elif wl.startswith("prefill"):
+        wl_p = wl
+    else:
+        wl_p = None
+    if wl_p:
+        cfg = gdn.workloads.config(3 if wl_p == "prefill_varlen16" else 4)
+        seqlens = list(cfg.seqlens)
+        if wl_p == "prefill_8x32768" and world > 1:
+            plan = gdn.sharding.plan_prefill(seqlens, 32, world)
+            seqlens = [seqlens[i] for i in plan[rank].seqs]
+        psets = prefill_sets(gdn, seqlens, 2, seed=rank, device="cuda", zero_state=cfg.zero_state)
+        psteps = max(3, min(20, args.steps // 100)) if not wl.startswith("prefill") else args.steps
+        pwarm = 2 if not wl.startswith("prefill") else args.warmup
+        sampler_p = ClockSampler(local) if wl.startswith("prefill") else None
+        pms, plaunch = time_steps(lambda s: prefill_call(gdn, s), psets, psteps, pwarm, world, sampler_p)
+        tokens = sum_over_ranks(sum(seqlens), world)
+        flops_launch = gdn.workloads.prefill_flops_per_token() * sum(seqlens)
+        pres = {"workload": wl_p, "tokens_per_s": tokens / (pms * 1e-3), "ms_per_step": pms,
+                "tokens_per_rank": sum(seqlens), "num_seqs_per_rank": len(seqlens),
+                "roofline": {"bound": "tensor", "achieved": flops_launch / (plaunch * 1e-3) / 1e12,
+                             "peak": bf16_peak, "unit": "TFLOP/s",
+                             "frac": flops_launch / (plaunch * 1e-3) / 1e12 / bf16_peak,
+                             "peak_kind": f"{peak_kind} bf16_tflops (burst)",
+                             "hbm_gbs": gdn.workloads.prefill_bytes(sum(seqlens), len(seqlens))
+                             / (plaunch * 1e-3) / 1e9,
+                             "traffic": profile_traffic("gdn_prefill_varlen16"),
+                             "avg_launch_us": plaunch * 1e3}}
+        if wl.startswith("prefill"):
+            result.update(metric="GDN prefill tokens/s", value=pres["tokens_per_s"], unit="tokens/s",
+                          ms_per_step=pms, dtype="bf16", config={"workload": wl_p, "seqlens_per_rank": seqlens,
+                                                                 "parallelism": f"dp{world}"},
+                          roofline=pres["roofline"], gpu_launches=psteps, clocks=sampler_p.summary(),
+                          e2e=None)
+        else:
+            result["prefill"] = pres
+        del psets
+    if rank == 0:
+        budget = float(os.environ.get("GDN_BENCH_CPU_BUDGET_S", "10"))
+        if world == 1 and budget > 0:
+            if wl.startswith("decode"):
+                v, sample, cores = cpu_decode_rate(gdn, 64 if wl == "decode_b64" else 1024, budget)
+                result["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
+                                          "sample": sample}
+            else:
+                v, sample, cores = cpu_prefill_rate(gdn, seqlens, budget)
+                result["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                          "sample": sample}
+        line = {"metric": result["metric"], "value": result["value"], "unit": result["unit"],
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": result["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": result["dtype"], "data": "synthetic (seeded, BASELINE distributions)",
+                **{k: v for k, v in result.items() if k not in ("metric", "value", "unit", "ms_per_step", "dtype")}}
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="decode_b64",
+                    choices=["decode_b64", "decode_b1024", "prefill_varlen16", "prefill_8x32768"])
+    ap.add_argument("--no-prefill", dest="prefill", action="store_false",
+                    help="skip the secondary configs[3] prefill measurement")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

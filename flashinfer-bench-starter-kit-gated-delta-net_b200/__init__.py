@@ -1,0 +1,16 @@
+"""gdn_b200 — B200-native Gated DeltaNet (GDN) decode and prefill operators.
+
+Drop-in for the two entry points of the reference solution
+(``solution/triton/kernel_decode.py::run`` and ``kernel_prefill.py::run``):
+the same tensors, dtypes, k-last fp32 state layout and value-returning
+``(output, new_state)`` contract, computed by hand-written sm_100a CUDA
+kernels in ``libgdn_b200.so`` reached through a C ABI (``include/gdn_b200.h``).
+There is no CPU or Triton fallback: without the built library on a CUDA
+device every operator raises.
+"""
+from . import workloads  # noqa: F401  (CPU-only helpers, always importable)
+from . import sharding  # noqa: F401
+from . import kernel_decode, kernel_prefill  # noqa: F401
+from ._lib import library, library_path  # noqa: F401
+
+__all__ = ["kernel_decode", "kernel_prefill", "workloads", "sharding", "library", "library_path"]

@@ -1,0 +1,250 @@
+// C ABI of libgdn_b200.so (declared in include/gdn_b200.h).
+//
+// Host-side argument validation, workspace sizing and kernel dispatch.  No
+// allocation, no synchronisation: every call only enqueues kernels on the
+// caller's stream.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/gdn_b200.h"
+#include "gdn_common.cuh"
+#include "gdn_kernels.h"
+
+namespace gdn {
+__device__ unsigned int g_gdn_device_error = 0;
+}
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return GDN_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(GDN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, int64_t stride_elems, int64_t stride2_elems, size_t elem, size_t align) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  return a % align == 0 && ((uint64_t)(stride_elems * (int64_t)elem)) % align == 0 &&
+         ((uint64_t)(stride2_elems * (int64_t)elem)) % align == 0;
+}
+
+// Byte extent [lo, hi) touched by a [n0, n1, 128, 128] fp32 tensor with strides (s0, s1).
+void state_extent(const float* p, int64_t n0, int64_t n1, int64_t s0, int64_t s1, uintptr_t& lo, uintptr_t& hi) {
+  const int64_t last = (n0 - 1) * s0 + (n1 - 1) * s1 + (int64_t)gdn::kHeadDim * gdn::kHeadDim;
+  lo = reinterpret_cast<uintptr_t>(p);
+  hi = lo + (uintptr_t)last * sizeof(float);
+}
+
+int check_common(int32_t HQ, int32_t HV, int32_t D) {
+  if (D != gdn::kHeadDim) return fail(GDN_ERR_UNSUPPORTED, "head_dim must be 128 (got %d)", D);
+  if (HQ <= 0 || HV <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "head counts must be positive (qk %d, v %d)", HQ, HV);
+  if (HV % HQ != 0)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "num_v_heads (%d) must be a multiple of num_qk_heads (%d)", HV, HQ);
+  return GDN_OK;
+}
+
+int check_state_pair(const float* state, int64_t s0, int64_t s1, const float* new_state, int64_t n0, int64_t n1,
+                     int64_t count, int32_t HV) {
+  if (!new_state) return fail(GDN_ERR_INVALID_ARGUMENT, "new_state must not be NULL");
+  if (!aligned(new_state, n0, n1, sizeof(float), 16))
+    return fail(GDN_ERR_UNSUPPORTED, "new_state rows must be 16-byte aligned (base and strides)");
+  if (state && !aligned(state, s0, s1, sizeof(float), 16))
+    return fail(GDN_ERR_UNSUPPORTED, "state rows must be 16-byte aligned (base and strides)");
+  if (n1 < 0 || n0 < 0 || s0 < 0 || s1 < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "negative state stride");
+  if (state && count > 0) {
+    uintptr_t alo, ahi, blo, bhi;
+    state_extent(state, count, HV, s0, s1, alo, ahi);
+    state_extent(new_state, count, HV, n0, n1, blo, bhi);
+    const bool overlap = alo < bhi && blo < ahi;
+    const bool identical = state == new_state && s0 == n0 && s1 == n1;
+    if (overlap && !identical)
+      return fail(GDN_ERR_INVALID_ARGUMENT, "new_state partially overlaps state (only exact aliasing is allowed)");
+  }
+  return GDN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_version(void) { return 100; }
+
+const char* gdn_last_error(void) { return g_last_error.c_str(); }
+
+int gdn_device_error(uint32_t* bits_out, int clear) {
+  unsigned int bits = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&bits, gdn::g_gdn_device_error, sizeof(bits));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  if (bits_out) *bits_out = bits;
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(gdn::g_gdn_device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  }
+  return ok();
+}
+
+int gdn_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k, int64_t k_stride_b,
+               int64_t k_stride_h, const void* v, int64_t v_stride_b, int64_t v_stride_h, const float* state,
+               int64_t state_stride_b, int64_t state_stride_h, const float* A_log, const void* a,
+               int64_t a_stride_b, const float* dt_bias, const void* b, int64_t b_stride_b, float scale, void* out,
+               int64_t out_stride_b, int64_t out_stride_h, float* new_state, int64_t new_state_stride_b,
+               int64_t new_state_stride_h, int32_t batch, int32_t num_qk_heads, int32_t num_v_heads,
+               int32_t head_dim, uint32_t flags, void* stream) {
+  int rc = check_common(num_qk_heads, num_v_heads, head_dim);
+  if (rc) return rc;
+  if (batch < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "batch must be >= 0 (got %d)", batch);
+  if (batch > 65535) return fail(GDN_ERR_UNSUPPORTED, "batch > 65535 per call is not supported (got %d)", batch);
+  if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
+  if (batch == 0) return ok();
+  if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !out)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "a required tensor pointer is NULL");
+  if (!aligned(q, q_stride_b, q_stride_h, 2, 8) || !aligned(k, k_stride_b, k_stride_h, 2, 8) ||
+      !aligned(v, v_stride_b, v_stride_h, 2, 8))
+    return fail(GDN_ERR_UNSUPPORTED, "q/k/v rows must be 8-byte aligned (base and strides)");
+  rc = check_state_pair(state, state_stride_b, state_stride_h, new_state, new_state_stride_b, new_state_stride_h,
+                        batch, num_v_heads);
+  if (rc) return rc;
+
+  gdn::DecodeParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.state = state;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.new_state = new_state;
+  p.q_sb = q_stride_b;
+  p.q_sh = q_stride_h;
+  p.k_sb = k_stride_b;
+  p.k_sh = k_stride_h;
+  p.v_sb = v_stride_b;
+  p.v_sh = v_stride_h;
+  p.s_sb = state_stride_b;
+  p.s_sh = state_stride_h;
+  p.a_sb = a_stride_b;
+  p.b_sb = b_stride_b;
+  p.o_sb = out_stride_b;
+  p.o_sh = out_stride_h;
+  p.n_sb = new_state_stride_b;
+  p.n_sh = new_state_stride_h;
+  p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim);
+  p.B = batch;
+  p.HQ = num_qk_heads;
+  p.HV = num_v_heads;
+  p.ratio = num_v_heads / num_qk_heads;
+  p.flags = flags;
+  const cudaError_t e =
+      gdn::launch_decode(p, gdn::decode_rows_for(batch, num_v_heads), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_decode launch");
+  return ok();
+}
+
+size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_t num_qk_heads, int32_t num_v_heads,
+                                  int32_t head_dim, uint32_t flags) {
+  (void)num_seqs;
+  (void)total_tokens;
+  (void)num_qk_heads;
+  (void)num_v_heads;
+  (void)head_dim;
+  (void)flags;
+  return 0;
+}
+
+int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h, const float* state,
+                int64_t state_stride_n, int64_t state_stride_h, const float* A_log, const void* a, int64_t a_stride_t,
+                const float* dt_bias, const void* b, int64_t b_stride_t, const void* cu_seqlens,
+                int32_t cu_seqlens_is_int64, float scale, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                float* new_state, int64_t new_state_stride_n, int64_t new_state_stride_h, int32_t num_seqs,
+                int64_t total_tokens, int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim, void* workspace,
+                size_t workspace_bytes, uint32_t flags, void* stream) {
+  int rc = check_common(num_qk_heads, num_v_heads, head_dim);
+  if (rc) return rc;
+  if (num_seqs < 0 || total_tokens < 0)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0 (got %d, %lld)", num_seqs,
+                (long long)total_tokens);
+  if (num_seqs > 65535) return fail(GDN_ERR_UNSUPPORTED, "num_seqs > 65535 per call is not supported");
+  if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
+  if (num_seqs == 0) return ok();
+  if (!cu_seqlens) return fail(GDN_ERR_INVALID_ARGUMENT, "cu_seqlens must not be NULL");
+  if (!A_log || !dt_bias) return fail(GDN_ERR_INVALID_ARGUMENT, "A_log and dt_bias must not be NULL");
+  if (total_tokens > 0) {
+    if (!q || !k || !v || !a || !b || !out)
+      return fail(GDN_ERR_INVALID_ARGUMENT, "a required tensor pointer is NULL");
+    if (!aligned(q, q_stride_t, q_stride_h, 2, 8) || !aligned(k, k_stride_t, k_stride_h, 2, 8) ||
+        !aligned(v, v_stride_t, v_stride_h, 2, 8))
+      return fail(GDN_ERR_UNSUPPORTED, "q/k/v rows must be 8-byte aligned (base and strides)");
+  }
+  rc = check_state_pair(state, state_stride_n, state_stride_h, new_state, new_state_stride_n, new_state_stride_h,
+                        num_seqs, num_v_heads);
+  if (rc) return rc;
+  const size_t need =
+      gdn_prefill_workspace_size(num_seqs, total_tokens, num_qk_heads, num_v_heads, head_dim, flags);
+  if (need > 0 && (!workspace || workspace_bytes < need))
+    return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+
+  gdn::PrefillParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.state = state;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.cu_seqlens = cu_seqlens;
+  p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.new_state = new_state;
+  p.q_st = q_stride_t;
+  p.q_sh = q_stride_h;
+  p.k_st = k_stride_t;
+  p.k_sh = k_stride_h;
+  p.v_st = v_stride_t;
+  p.v_sh = v_stride_h;
+  p.s_sn = state_stride_n;
+  p.s_sh = state_stride_h;
+  p.a_st = a_stride_t;
+  p.b_st = b_stride_t;
+  p.o_st = out_stride_t;
+  p.o_sh = out_stride_h;
+  p.n_sn = new_state_stride_n;
+  p.n_sh = new_state_stride_h;
+  p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim);
+  p.N = num_seqs;
+  p.HQ = num_qk_heads;
+  p.HV = num_v_heads;
+  p.ratio = num_v_heads / num_qk_heads;
+  p.T = total_tokens;
+  p.flags = flags;
+  p.workspace = workspace;
+  p.workspace_bytes = workspace_bytes;
+  const cudaError_t e = gdn::launch_prefill_serial(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill launch");
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,65 @@
+// Internal launch interface between the C ABI (gdn_abi.cu) and the kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr uint32_t kFlagQkL2Norm = 1u;  // mirrors GDN_FLAG_QK_L2NORM
+
+// Strides are in elements; the innermost (feature) stride is 1 for every tensor.
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const float* state;  // nullptr -> zero initial state
+  const float* A_log;
+  const __nv_bfloat16* a;
+  const float* dt_bias;
+  const __nv_bfloat16* b;
+  __nv_bfloat16* out;
+  float* new_state;
+  int64_t q_sb, q_sh, k_sb, k_sh, v_sb, v_sh;
+  int64_t s_sb, s_sh;  // state: [B, HV, 128, 128], rows contiguous
+  int64_t a_sb, b_sb;  // a, b: [B, HV] (head stride 1)
+  int64_t o_sb, o_sh;  // out: [B, HV, 128]
+  int64_t n_sb, n_sh;  // new_state: [B, HV, 128, 128], rows contiguous
+  float scale;
+  int B, HQ, HV, ratio;
+  uint32_t flags;
+};
+
+struct PrefillParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const float* state;  // nullptr -> zero initial state
+  const float* A_log;
+  const __nv_bfloat16* a;
+  const float* dt_bias;
+  const __nv_bfloat16* b;
+  const void* cu_seqlens;  // [N + 1], int32 or int64 (device)
+  int cu_is_int64;
+  __nv_bfloat16* out;
+  float* new_state;
+  int64_t q_st, q_sh, k_st, k_sh, v_st, v_sh;
+  int64_t s_sn, s_sh;
+  int64_t a_st, b_st;
+  int64_t o_st, o_sh;
+  int64_t n_sn, n_sh;
+  float scale;
+  int N, HQ, HV, ratio;
+  int64_t T;
+  uint32_t flags;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+int decode_rows_for(int B, int HV);
+cudaError_t launch_decode(const DecodeParams& p, int rows, cudaStream_t stream);
+
+cudaError_t launch_prefill_serial(const PrefillParams& p, cudaStream_t stream);
+
+}  // namespace gdn

@@ -1,0 +1,112 @@
+"""GDN varlen prefill operator — drop-in for ``solution/triton/kernel_prefill.py::run``.
+
+``run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale) -> (output, new_state)``
+keeps the reference entry point's signature, shapes, dtypes, k-last state
+layout and value-returning style (``kernel_prefill.py:234``):
+
+  q, k       bf16 [T, HQ, 128]       v      bf16 [T, HV, 128]
+  state      fp32 [N, HV, 128, 128] or None (zeros)
+  A_log      fp32 [HV]               dt_bias fp32 [HV]
+  a, b       bf16 [T, HV]            cu_seqlens int32/int64 [N + 1] (on the device)
+  scale      float, None or 0 -> 1/sqrt(128)
+  output     bf16 [T, HV, 128]       new_state fp32 [N, HV, 128, 128] (new buffer)
+
+An empty sequence passes its initial state through, as the reference kernel
+does (``kernel_prefill.py:65-73``).  ``run_dps`` is the destination-passing
+form.  The work runs in sm_100a kernels through the C ABI ``gdn_prefill`` on
+the current CUDA stream (no host synchronisation, no CPU compute).
+"""
+from __future__ import annotations
+
+import math
+import sys
+from pathlib import Path
+
+import torch
+
+if __package__ in (None, ""):  # loaded by file path: register the package first
+    import importlib.util
+
+    _dir = Path(__file__).resolve().parent
+    if "gdn_b200" not in sys.modules:
+        _spec = importlib.util.spec_from_file_location(
+            "gdn_b200", _dir / "__init__.py", submodule_search_locations=[str(_dir)])
+        _mod = importlib.util.module_from_spec(_spec)
+        sys.modules["gdn_b200"] = _mod
+        _spec.loader.exec_module(_mod)
+    from gdn_b200 import _lib
+    from gdn_b200._tensors import check_cuda, ptr, stream_handle, inner_contig, seq_head_strides
+else:
+    from . import _lib
+    from ._tensors import check_cuda, ptr, stream_handle, inner_contig, seq_head_strides
+
+# Workspace buffers cached per (device, stream) so repeated calls do not allocate.
+_workspaces: dict = {}
+
+
+def workspace_size(num_seqs: int, total_tokens: int, num_qk_heads: int, num_v_heads: int,
+                   head_dim: int = 128, use_qk_l2norm: bool = False) -> int:
+    flags = _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0
+    return int(_lib.library().gdn_prefill_workspace_size(num_seqs, total_tokens, num_qk_heads,
+                                                         num_v_heads, head_dim, flags))
+
+
+def _workspace(device, nbytes: int):
+    if nbytes == 0:
+        return None
+    key = (device, torch.cuda.current_stream(device).cuda_stream)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
+def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
+            use_qk_l2norm: bool = False, workspace=None):
+    """Destination-passing prefill: writes ``output`` [T,HV,128] bf16 and
+    ``new_state`` [N,HV,128,128] fp32 (which may be ``state`` itself)."""
+    T, HQ, D = q.shape
+    HV = v.shape[1]
+    N = cu_seqlens.shape[0] - 1
+    check_cuda(q, k, v, A_log, a, dt_bias, b, output, new_state, state=state)
+    if cu_seqlens.device != q.device:
+        raise ValueError("cu_seqlens must be on the same device as q")
+    if cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
+    if scale is None or scale == 0.0:
+        scale = 1.0 / math.sqrt(D)
+    q, k, v = inner_contig(q), inner_contig(k), inner_contig(v)
+    a, b = inner_contig(a), inner_contig(b)
+    A_log, dt_bias, cu = A_log.contiguous(), dt_bias.contiguous(), cu_seqlens.contiguous()
+    if state is not None and not state.is_contiguous() and state is not new_state:
+        state = state.contiguous()
+    flags = _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0
+    lib = _lib.library()
+    need = int(lib.gdn_prefill_workspace_size(N, T, HQ, HV, D, flags))
+    if workspace is None:
+        workspace = _workspace(q.device, need)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = lib.gdn_prefill(ptr(q), *seq_head_strides(q, 0, 1), ptr(k), *seq_head_strides(k, 0, 1),
+                         ptr(v), *seq_head_strides(v, 0, 1),
+                         ptr(state), *(seq_head_strides(state, 0, 1) if state is not None else (0, 0)),
+                         ptr(A_log), ptr(a), a.stride(0), ptr(dt_bias), ptr(b), b.stride(0),
+                         ptr(cu), int(cu.dtype == torch.int64),
+                         float(scale),
+                         ptr(output), *seq_head_strides(output, 0, 1),
+                         ptr(new_state), *seq_head_strides(new_state, 0, 1),
+                         N, T, HQ, HV, D, ptr(workspace), ws_bytes, flags, stream_handle(q.device))
+    _lib.check(rc)
+    return output, new_state
+
+
+def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2norm: bool = False):
+    """Value-returning prefill (the reference's ``run``): returns
+    ``(output [T,HV,128] bf16, new_state [N,HV,128,128] fp32)``."""
+    T, _, D = q.shape
+    HV = v.shape[1]
+    N = cu_seqlens.shape[0] - 1
+    output = torch.empty(T, HV, D, dtype=torch.bfloat16, device=q.device)
+    new_state = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
+    return run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                   use_qk_l2norm=use_qk_l2norm)

@@ -1,0 +1,137 @@
+/*
+ * gdn_b200 — C ABI of the B200-native Gated DeltaNet (GDN) operators.
+ *
+ * Library: libgdn_b200.so (built for sm_100a).  Every entry point is
+ * asynchronous on the given CUDA stream (a cudaStream_t passed as void*; NULL
+ * means the legacy default stream), performs no host<->device
+ * synchronisation, and returns GDN_OK or an error code; the message of the
+ * last failure on the calling thread is available from gdn_last_error().
+ *
+ * Tensor conventions (all device pointers, innermost dimension contiguous,
+ * strides given in ELEMENTS):
+ *   bf16 tensors   q, k, v, a, b, out (passed as void*: raw bf16 storage)
+ *   fp32 tensors   state, new_state, A_log, dt_bias
+ *   state layout   "k-last" [.., HV, V = head_dim, K = head_dim]; each 128-float
+ *                  row is contiguous and rows of one head are adjacent, so only
+ *                  the sequence and head strides are passed.
+ *   GVA mapping    v-head h reads q/k head h / (num_v_heads / num_qk_heads).
+ *   scale          <= 0 selects 1 / sqrt(head_dim).
+ *   state == NULL  zero initial state.
+ *   new_state      may alias state exactly (in-place update); partial overlap
+ *                  is rejected.
+ * Alignment: q, k and v rows must start on 8-byte boundaries and state /
+ * new_state rows on 16-byte boundaries (GDN_ERR_UNSUPPORTED otherwise).
+ * head_dim must be 128 (the definitions' fixed head size).
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_OK 0
+#define GDN_ERR_INVALID_ARGUMENT 1 /* shapes, strides, null pointers, overlap */
+#define GDN_ERR_UNSUPPORTED 2      /* valid but not implemented (head_dim != 128, alignment) */
+#define GDN_ERR_CUDA 3             /* a CUDA runtime call or kernel launch failed */
+#define GDN_ERR_WORKSPACE 4        /* workspace missing or too small */
+
+#define GDN_FLAG_QK_L2NORM 0x1u /* L2-normalise q and k inside the kernel (eps 1e-6); default off */
+
+/* Device-side error bits reported by gdn_device_error(). */
+#define GDN_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded wait inside a kernel gave up */
+#define GDN_DEVERR_BAD_SEQLENS 0x2u  /* cu_seqlens not monotone or beyond total_tokens */
+
+/* Version of this ABI (major * 10000 + minor * 100 + patch). */
+GDN_API int gdn_version(void);
+
+/* Message describing the last failure on the calling thread ("" if none). */
+GDN_API const char* gdn_last_error(void);
+
+/*
+ * Reads (and optionally clears) the device-side error word of the current
+ * device.  Synchronous: waits for prior work on the device.  For tests and
+ * debugging only; the operator entry points never call it.
+ */
+GDN_API int gdn_device_error(uint32_t* bits_out, int clear);
+
+/*
+ * Single-token decode step.
+ * Replaces solution/triton/kernel_decode.py:186 run(q, k, v, state, A_log, a,
+ * dt_bias, b, scale) and its launcher decode_kernel (kernel_decode.py:115-183),
+ * whose strides (kernel_decode.py:21-36) it takes the same way.
+ *   q, k       [B, 1, num_qk_heads, head_dim]   strides (q_stride_b, q_stride_h)
+ *   v          [B, 1, num_v_heads, head_dim]    strides (v_stride_b, v_stride_h)
+ *   state      [B, num_v_heads, head_dim, head_dim] fp32 or NULL
+ *   a, b       [B, 1, num_v_heads] bf16, head stride 1, batch strides a_stride_b, b_stride_b
+ *   A_log, dt_bias  [num_v_heads] fp32
+ *   out        [B, 1, num_v_heads, head_dim] bf16   strides (out_stride_b, out_stride_h)
+ *   new_state  same shape as state                  strides (new_state_stride_b, new_state_stride_h)
+ */
+GDN_API int gdn_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                       const void* k, int64_t k_stride_b, int64_t k_stride_h,
+               const void* v, int64_t v_stride_b, int64_t v_stride_h,
+               const float* state, int64_t state_stride_b, int64_t state_stride_h,
+               const float* A_log,
+               const void* a, int64_t a_stride_b,
+               const float* dt_bias,
+               const void* b, int64_t b_stride_b,
+               float scale,
+               void* out, int64_t out_stride_b, int64_t out_stride_h,
+               float* new_state, int64_t new_state_stride_b, int64_t new_state_stride_h,
+               int32_t batch, int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+               uint32_t flags, void* stream);
+
+/*
+ * Variable-length prefill.
+ * Replaces solution/triton/kernel_prefill.py:234 run(q, k, v, state, A_log, a,
+ * dt_bias, b, cu_seqlens, scale) and its launcher run_prefill
+ * (kernel_prefill.py:156-231).
+ *   q, k       [T, num_qk_heads, head_dim]      strides (q_stride_t, q_stride_h)
+ *   v          [T, num_v_heads, head_dim]       strides (v_stride_t, v_stride_h)
+ *   state      [N, num_v_heads, head_dim, head_dim] fp32 or NULL
+ *   a, b       [T, num_v_heads] bf16, head stride 1
+ *   cu_seqlens [N + 1] device int32 (cu_seqlens_is_int64 = 0) or int64 (= 1);
+ *              monotone, cu_seqlens[0] >= 0, cu_seqlens[N] <= total_tokens
+ *              (checked on the device: GDN_DEVERR_BAD_SEQLENS).
+ *   out        [T, num_v_heads, head_dim] bf16
+ *   new_state  [N, num_v_heads, head_dim, head_dim] fp32
+ *   An empty sequence passes its initial state through (kernel_prefill.py:65-73).
+ *   workspace  device scratch of at least gdn_prefill_workspace_size(...) bytes
+ *              (may be NULL when that size is 0).
+ */
+GDN_API int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                const void* k, int64_t k_stride_t, int64_t k_stride_h,
+                const void* v, int64_t v_stride_t, int64_t v_stride_h,
+                const float* state, int64_t state_stride_n, int64_t state_stride_h,
+                const float* A_log,
+                const void* a, int64_t a_stride_t,
+                const float* dt_bias,
+                const void* b, int64_t b_stride_t,
+                const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                float scale,
+                void* out, int64_t out_stride_t, int64_t out_stride_h,
+                float* new_state, int64_t new_state_stride_n, int64_t new_state_stride_h,
+                int32_t num_seqs, int64_t total_tokens,
+                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                void* workspace, size_t workspace_bytes,
+                uint32_t flags, void* stream);
+
+/* Bytes of device workspace gdn_prefill needs for this problem size. */
+GDN_API size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                                  int32_t num_v_heads, int32_t head_dim, uint32_t flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

@@ -1,0 +1,107 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Runs the reference solution's own Triton kernels
+(``solution/triton/kernel_decode.py::run`` and ``kernel_prefill.py::run``) on
+the CPU under ``TRITON_INTERPRET=1``, plus the definition's torch reference
+recurrence shipped with ``flashinfer==0.6.11.post2``
+(``flashinfer/trace/templates/gdn.py``: ``_gdn_decode_reference``,
+``_gdn_prefill_reference``), on small seeded inputs, and stores inputs and
+outputs as compressed ``.npz`` files (the torch reference's states are kept
+only as their max difference from the Triton kernels' states, to keep the
+fixtures small).  bf16 tensors are stored as uint16 bit
+patterns; the initial states are drawn as bf16-representable fp32 values so
+they can be stored as uint16 too.
+
+Usage (needs the reference checkout; not run by the tests):
+    python tests/golden/make_golden.py /path/to/reference
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+os.environ["TRITON_INTERPRET"] = "1"
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = Path(__file__).resolve().parent
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def make_inputs(shape_q, shape_v, shape_g, state_shape, seed):
+    gen = torch.Generator()
+    gen.manual_seed(seed)
+
+    def unit(shape):
+        x = torch.randn(*shape, generator=gen)
+        return (x / x.norm(dim=-1, keepdim=True)).bfloat16()
+
+    q, k = unit(shape_q), unit(shape_q)
+    v = torch.randn(*shape_v, generator=gen).bfloat16()
+    a = torch.randn(*shape_g, generator=gen).bfloat16()
+    b = torch.randn(*shape_g, generator=gen).bfloat16()
+    HV = shape_v[-2]
+    A_log = torch.rand(HV, generator=gen) * 1.5
+    dt_bias = torch.rand(HV, generator=gen) * 2 - 1
+    state = (torch.randn(*state_shape, generator=gen) * 0.05).bfloat16().float()
+    return q, k, v, a, b, A_log, dt_bias, state
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, str(Path(ref_root) / "solution" / "triton"))
+    import kernel_decode  # reference decode entry point
+    import kernel_prefill  # reference prefill entry point
+    from flashinfer.trace.templates.gdn import _gdn_decode_reference, _gdn_prefill_reference
+
+    # ---- decode, the reference definition's own head counts (qk4 / v8) ----
+    cases = [("decode_qk4v8_b3", 3, 4, 8, 11, True, None),
+             ("decode_qk4v8_b2_nostate", 2, 4, 8, 12, False, 0.25)]
+    for name, B, HQ, HV, seed, with_state, scale in cases:
+        q, k, v, a, b, A_log, dt_bias, state = make_inputs(
+            (B, 1, HQ, 128), (B, 1, HV, 128), (B, 1, HV), (B, HV, 128, 128), seed)
+        st = state if with_state else None
+        o_tr, s_tr = kernel_decode.run(q, k, v, st, A_log, a, dt_bias, b, scale)
+        o_fi, s_fi = _gdn_decode_reference(q, k, v, st, A_log, a, dt_bias, b, scale)
+        np.savez_compressed(
+            HERE / f"{name}.npz", q=bits(q), k=bits(k), v=bits(v), a=bits(a), b=bits(b),
+            A_log=A_log.numpy(), dt_bias=dt_bias.numpy(),
+            state=bits(state.bfloat16()) if with_state else np.zeros(0, np.uint16),
+            has_state=np.array(with_state), scale=np.float32(0.0 if scale is None else scale),
+            out_triton=bits(o_tr), new_state_triton=s_tr.numpy(),
+            out_torchref=bits(o_fi),
+            torchref_state_maxdiff=np.float32((s_tr - s_fi).abs().max().item()))
+        print(name, "triton vs torch-ref: out", (o_tr.float() - o_fi.float()).abs().max().item(),
+              "state", (s_tr - s_fi).abs().max().item())
+
+    # ---- prefill: an empty sequence, a 1-token one, and one crossing the 64-token chunk ----
+    lens = [1, 0, 70]
+    HQ, HV = 4, 8
+    T, N = sum(lens), len(lens)
+    q, k, v, a, b, A_log, dt_bias, state = make_inputs(
+        (T, HQ, 128), (T, HV, 128), (T, HV), (N, HV, 128, 128), 21)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    o_tr, s_tr = kernel_prefill.run(q, k, v, state, A_log, a, dt_bias, b, cu, None)
+    o_fi, s_fi = _gdn_prefill_reference(q, k, v, state, A_log, a, dt_bias, b, cu, None)
+    np.savez_compressed(
+        HERE / "prefill_qk4v8_lens1-0-70.npz", q=bits(q), k=bits(k), v=bits(v), a=bits(a),
+        b=bits(b), A_log=A_log.numpy(), dt_bias=dt_bias.numpy(), state=bits(state.bfloat16()),
+        cu_seqlens=cu.numpy(), out_triton=bits(o_tr), new_state_triton=s_tr.numpy(),
+        out_torchref=bits(o_fi),
+        torchref_state_maxdiff_nonempty=np.float32(
+            max((s_tr[i] - s_fi[i]).abs().max().item() for i in (0, 2))),
+        torchref_empty_seq_state_absmax=np.float32(s_fi[1].abs().max().item()))
+    print("prefill triton vs torch-ref: out", (o_tr.float() - o_fi.float()).abs().max().item(),
+          "state (non-empty seqs)", max((s_tr[i] - s_fi[i]).abs().max().item() for i in (0, 2)),
+          "empty-seq state: triton passes through", (s_tr[1] - state[1]).abs().max().item(),
+          "torch-ref writes zeros", s_fi[1].abs().max().item())
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference checkout>")
+    main(sys.argv[1])

@@ -1,0 +1,111 @@
+"""The C-ABI library loads and exports every symbol ``include/gdn_b200.h``
+declares; host-side validation rejects bad arguments before any launch.
+CPU only: no call here reaches a kernel."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "gdn_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib(gdn):
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_gdn_build", Path(gdn.__file__).parent / "build.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.build()
+    return gdn._lib.library()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return re.findall(r"GDN_API\s+[\w\s\*]+?\b(gdn_\w+)\s*\(", text)
+
+
+def test_header_declares_expected_entry_points():
+    names = set(declared_functions())
+    assert {"gdn_decode", "gdn_prefill", "gdn_prefill_workspace_size", "gdn_last_error",
+            "gdn_device_error", "gdn_version"} <= names
+
+
+def test_library_exports_every_declared_symbol(lib, gdn):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in gdn._lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version(lib):
+    assert lib.gdn_version() >= 100
+
+
+def _decode_call(lib, **over):
+    args = dict(q=8, k=8, v=8, state=None, A_log=16, a=8, dt_bias=16, b=8, out=8, new_state=16,
+                B=1, HQ=16, HV=32, D=128, flags=0, qs=(2048, 128), ss=(32 * 16384, 16384))
+    args.update(over)
+    return lib.gdn_decode(args["q"], *args["qs"], args["k"], *args["qs"], args["v"], 4096, 128,
+                          args["state"], *args["ss"], args["A_log"], args["a"], 32, args["dt_bias"],
+                          args["b"], 32, 0.0, args["out"], 4096, 128, args["new_state"], *args["ss"],
+                          args["B"], args["HQ"], args["HV"], args["D"], args["flags"], None)
+
+
+@pytest.mark.parametrize("over,code,needle", [
+    (dict(D=64), 2, "head_dim"),
+    (dict(HV=24), 1, "multiple"),
+    (dict(HQ=0), 1, "positive"),
+    (dict(B=-1), 1, "batch"),
+    (dict(flags=0x80), 1, "flag"),
+    (dict(q=None), 1, "NULL"),
+    (dict(new_state=None), 1, "new_state"),
+    (dict(q=6), 2, "aligned"),
+    (dict(new_state=8), 2, "16-byte"),
+    (dict(state=16, new_state=16 + 64), 1, "overlap"),
+])
+def test_decode_rejects_bad_arguments(lib, over, code, needle):
+    rc = _decode_call(lib, **over)
+    assert rc == code
+    assert needle in lib.gdn_last_error().decode()
+
+
+def test_decode_batch_zero_is_a_no_op(lib):
+    assert _decode_call(lib, B=0, q=None) == 0
+    assert lib.gdn_last_error() == b""
+
+
+def test_prefill_rejects_bad_arguments(lib):
+    def call(**over):
+        a = dict(cu=8, N=2, T=10, HQ=16, HV=32, D=128, ws=None, wsb=0, new_state=16)
+        a.update(over)
+        return lib.gdn_prefill(8, 2048, 128, 8, 2048, 128, 8, 4096, 128, None, 0, 0, 16, 8, 32, 16, 8, 32,
+                               a["cu"], 0, 0.0, 8, 4096, 128, a["new_state"], 32 * 16384, 16384,
+                               a["N"], a["T"], a["HQ"], a["HV"], a["D"], a["ws"], a["wsb"], 0, None)
+    assert call(cu=None) == 1 and "cu_seqlens" in lib.gdn_last_error().decode()
+    assert call(N=-1) == 1
+    assert call(D=256) == 2
+    assert call(N=0) == 0
+
+
+def test_workspace_size_is_deterministic(lib):
+    a = lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
+    assert a == lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
+
+
+def test_missing_library_fails_loudly(gdn, monkeypatch, tmp_path):
+    monkeypatch.setattr(gdn._lib, "_lib", None)
+    monkeypatch.setenv("GDN_B200_LIB", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="not built"):
+        gdn._lib.library()
+
+
+def test_cpu_tensors_are_rejected(gdn):
+    import torch
+
+    inp = gdn.workloads.decode_inputs(1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        gdn.kernel_decode.run(**inp)

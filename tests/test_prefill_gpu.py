@@ -1,0 +1,117 @@
+"""Varlen prefill parity on the GPU (through the C ABI) against the reference
+kernel's golden vectors and the CPU oracle.  Tolerances as in the decode tests:
+bf16 output atol = rtol = 1e-2; final fp32 state within 1e-3 relative."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, state_close
+from oracle import c_oracle
+from oracle import gdn_oracle as ref
+
+pytestmark = pytest.mark.gpu
+OUT_TOL = dict(atol=1e-2, rtol=1e-2)
+STATE_RTOL = 1e-3
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def to_dev(inp):
+    return {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in inp.items()}
+
+
+def oracle_prefill(inp, impl=ref, **kw):
+    st = inp["state"]
+    return impl.prefill(bits(inp["q"]), bits(inp["k"]), bits(inp["v"]),
+                        None if st is None else st.cpu().numpy(), inp["A_log"].cpu().numpy(),
+                        bits(inp["a"]), inp["dt_bias"].cpu().numpy(), bits(inp["b"]),
+                        inp["cu_seqlens"].cpu().numpy(), inp["scale"], **kw)
+
+
+def assert_match(out, new_state, o_ref_bits, s_ref):
+    o = out.float().cpu().numpy()
+    np.testing.assert_allclose(o, ref.bf16_bits_to_f32(o_ref_bits), **OUT_TOL)
+    ok, err = state_close(new_state.cpu().numpy(), s_ref, STATE_RTOL)
+    assert ok, f"state rel err {err}"
+
+
+def test_golden_reference_kernel(gdn):
+    g = load_golden("prefill_qk4v8_lens1-0-70")
+    tb = lambda x: torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).cuda()  # noqa: E731
+    state = torch.from_numpy(ref.bf16_bits_to_f32(g["state"])).cuda()
+    out, ns = gdn.kernel_prefill.run(tb(g["q"]), tb(g["k"]), tb(g["v"]), state,
+                                     torch.from_numpy(g["A_log"]).cuda(), tb(g["a"]),
+                                     torch.from_numpy(g["dt_bias"]).cuda(), tb(g["b"]),
+                                     torch.from_numpy(g["cu_seqlens"]).cuda(), None)
+    torch.cuda.synchronize()
+    assert_match(out, ns, g["out_triton"], g["new_state_triton"])
+    # empty sequence: initial state passes through unchanged
+    assert torch.equal(ns[1], state[1])
+
+
+@pytest.mark.parametrize("lens", [[1], [64], [65], [1, 0, 63, 64, 65, 130], [0, 0], [200, 3, 129]])
+def test_random_varlen(gdn, lens):
+    inp = gdn.workloads.prefill_inputs(lens, seed=sum(lens) + len(lens))
+    out, ns = gdn.kernel_prefill.run(**to_dev(inp))
+    o_ref, s_ref = oracle_prefill(inp)
+    assert_match(out, ns, o_ref, s_ref)
+    assert gdn._lib.device_error() == 0
+
+
+def test_int64_cu_seqlens_zero_state(gdn):
+    inp = gdn.workloads.prefill_inputs([70, 5], seed=31, cu_dtype=torch.int64)
+    inp["state"] = None
+    out, ns = gdn.kernel_prefill.run(**to_dev(inp))
+    o_ref, s_ref = oracle_prefill(inp)
+    assert_match(out, ns, o_ref, s_ref)
+
+
+def test_qk_l2norm_and_gva_ratio_4(gdn):
+    inp = gdn.workloads.prefill_inputs([40, 77], num_qk_heads=8, seed=32)
+    inp["q"] = (inp["q"].float() * 2.0).bfloat16()
+    out, ns = gdn.kernel_prefill.run(**to_dev(inp), use_qk_l2norm=True)
+    o_ref, s_ref = oracle_prefill(inp, use_qk_l2norm=True)
+    assert_match(out, ns, o_ref, s_ref)
+
+
+def test_in_place_state(gdn):
+    inp = gdn.workloads.prefill_inputs([33, 96], seed=33)
+    d = to_dev(inp)
+    st = d["state"].clone()
+    out = torch.empty(129, 32, 128, dtype=torch.bfloat16, device="cuda")
+    gdn.kernel_prefill.run_dps(d["q"], d["k"], d["v"], st, d["A_log"], d["a"], d["dt_bias"], d["b"],
+                               d["cu_seqlens"], None, out, st)
+    o_ref, s_ref = oracle_prefill(inp)
+    assert_match(out, st, o_ref, s_ref)
+
+
+def test_varlen16_full_size_subset(gdn):
+    """configs[3] at full size on the GPU; the shortest and longest sequences are
+    re-run alone and checked against the C oracle (sequences are independent)."""
+    lens = gdn.workloads.varlen_seqlens()
+    inp = gdn.workloads.prefill_inputs(lens, seed=0, device="cuda")
+    out, ns = gdn.kernel_prefill.run(**inp)
+    torch.cuda.synchronize()
+    cu = inp["cu_seqlens"].cpu().tolist()
+    for i in (int(np.argmin(lens)), int(np.argmax(lens))):
+        t0, t1 = cu[i], cu[i + 1]
+        sub = dict(inp)
+        for key in ("q", "k", "v", "a", "b"):
+            sub[key] = inp[key][t0:t1].cpu()
+        sub["state"] = inp["state"][i:i + 1].cpu()
+        sub["cu_seqlens"] = torch.tensor([0, t1 - t0], dtype=torch.int32)
+        sub["A_log"], sub["dt_bias"] = inp["A_log"].cpu(), inp["dt_bias"].cpu()
+        o_ref, s_ref = oracle_prefill(sub, impl=c_oracle)
+        assert_match(out[t0:t1], ns[i:i + 1], o_ref, s_ref)
+
+
+def test_bad_cu_seqlens_sets_device_error(gdn):
+    inp = to_dev(gdn.workloads.prefill_inputs([8, 8], seed=34))
+    inp["cu_seqlens"] = torch.tensor([0, 12, 9], dtype=torch.int32, device="cuda")  # not monotone
+    gdn._lib.device_error(clear=True)
+    gdn.kernel_prefill.run(**inp)
+    assert gdn._lib.device_error(clear=True) & gdn._lib.GDN_DEVERR_BAD_SEQLENS
