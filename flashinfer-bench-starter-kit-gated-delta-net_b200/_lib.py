@@ -19,6 +19,7 @@ GDN_ERR_UNSUPPORTED = 2
 GDN_ERR_CUDA = 3
 GDN_ERR_WORKSPACE = 4
 GDN_FLAG_QK_L2NORM = 0x1
+GDN_FLAG_PREFILL_SERIAL = 0x2
 GDN_DEVERR_WAIT_TIMEOUT = 0x1
 GDN_DEVERR_BAD_SEQLENS = 0x2
 

@@ -187,7 +187,8 @@ int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const voi
     return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0 (got %d, %lld)", num_seqs,
                 (long long)total_tokens);
   if (num_seqs > 65535) return fail(GDN_ERR_UNSUPPORTED, "num_seqs > 65535 per call is not supported");
-  if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
+  if (flags & ~(GDN_FLAG_QK_L2NORM | GDN_FLAG_PREFILL_SERIAL))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
   if (num_seqs == 0) return ok();
   if (!cu_seqlens) return fail(GDN_ERR_INVALID_ARGUMENT, "cu_seqlens must not be NULL");
   if (!A_log || !dt_bias) return fail(GDN_ERR_INVALID_ARGUMENT, "A_log and dt_bias must not be NULL");
@@ -242,8 +243,10 @@ int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const voi
   p.flags = flags;
   p.workspace = workspace;
   p.workspace_bytes = workspace_bytes;
-  const cudaError_t e = gdn::launch_prefill_serial(p, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill launch");
+  const bool chunked = !(flags & GDN_FLAG_PREFILL_SERIAL) && gdn::prefill_chunk_supported(p);
+  const cudaError_t e = chunked ? gdn::launch_prefill_chunk(p, static_cast<cudaStream_t>(stream))
+                                : gdn::launch_prefill_serial(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, chunked ? "gdn_prefill (chunked) launch" : "gdn_prefill launch");
   return ok();
 }
 

@@ -7,7 +7,8 @@
 
 namespace gdn {
 
-constexpr uint32_t kFlagQkL2Norm = 1u;  // mirrors GDN_FLAG_QK_L2NORM
+constexpr uint32_t kFlagQkL2Norm = 1u;        // mirrors GDN_FLAG_QK_L2NORM
+constexpr uint32_t kFlagPrefillSerial = 2u;   // mirrors GDN_FLAG_PREFILL_SERIAL
 
 // Strides are in elements; the innermost (feature) stride is 1 for every tensor.
 struct DecodeParams {
@@ -61,5 +62,10 @@ int decode_rows_for(int B, int HV);
 cudaError_t launch_decode(const DecodeParams& p, int rows, cudaStream_t stream);
 
 cudaError_t launch_prefill_serial(const PrefillParams& p, cudaStream_t stream);
+
+// Chunked tensor-core prefill: usable when q/k/v rows and strides are 16-byte
+// aligned (TMA) and no in-kernel q/k normalisation is requested.
+bool prefill_chunk_supported(const PrefillParams& p);
+cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream);
 
 }  // namespace gdn

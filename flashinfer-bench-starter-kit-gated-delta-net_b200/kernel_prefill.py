@@ -63,9 +63,13 @@ def _workspace(device, nbytes: int):
 
 
 def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
-            use_qk_l2norm: bool = False, workspace=None):
+            use_qk_l2norm: bool = False, serial: bool = False, workspace=None):
     """Destination-passing prefill: writes ``output`` [T,HV,128] bf16 and
-    ``new_state`` [N,HV,128,128] fp32 (which may be ``state`` itself)."""
+    ``new_state`` [N,HV,128,128] fp32 (which may be ``state`` itself).
+
+    The chunked tensor-core kernel runs whenever q/k/v rows and strides are
+    16-byte aligned and ``use_qk_l2norm`` is off; otherwise (or with
+    ``serial=True``, a cross-checking switch) the token-serial CUDA kernel runs."""
     T, HQ, D = q.shape
     HV = v.shape[1]
     N = cu_seqlens.shape[0] - 1
@@ -81,7 +85,7 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     A_log, dt_bias, cu = A_log.contiguous(), dt_bias.contiguous(), cu_seqlens.contiguous()
     if state is not None and not state.is_contiguous() and state is not new_state:
         state = state.contiguous()
-    flags = _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0
+    flags = (_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0) | (_lib.GDN_FLAG_PREFILL_SERIAL if serial else 0)
     lib = _lib.library()
     need = int(lib.gdn_prefill_workspace_size(N, T, HQ, HV, D, flags))
     if workspace is None:
@@ -100,7 +104,8 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     return output, new_state
 
 
-def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2norm: bool = False):
+def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2norm: bool = False,
+        serial: bool = False):
     """Value-returning prefill (the reference's ``run``): returns
     ``(output [T,HV,128] bf16, new_state [N,HV,128,128] fp32)``."""
     T, _, D = q.shape
@@ -109,4 +114,4 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
     output = torch.empty(T, HV, D, dtype=torch.bfloat16, device=q.device)
     new_state = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
     return run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
-                   use_qk_l2norm=use_qk_l2norm)
+                   use_qk_l2norm=use_qk_l2norm, serial=serial)

@@ -45,7 +45,9 @@ extern "C" {
 #define GDN_ERR_CUDA 3             /* a CUDA runtime call or kernel launch failed */
 #define GDN_ERR_WORKSPACE 4        /* workspace missing or too small */
 
-#define GDN_FLAG_QK_L2NORM 0x1u /* L2-normalise q and k inside the kernel (eps 1e-6); default off */
+#define GDN_FLAG_QK_L2NORM 0x1u      /* L2-normalise q and k inside the kernel (eps 1e-6); default off */
+#define GDN_FLAG_PREFILL_SERIAL 0x2u /* prefill: use the token-serial kernel instead of the chunked
+                                        tensor-core kernel (cross-checking; prefill only) */
 
 /* Device-side error bits reported by gdn_device_error(). */
 #define GDN_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded wait inside a kernel gave up */

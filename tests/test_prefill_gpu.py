@@ -115,3 +115,34 @@ def test_bad_cu_seqlens_sets_device_error(gdn):
     gdn._lib.device_error(clear=True)
     gdn.kernel_prefill.run(**inp)
     assert gdn._lib.device_error(clear=True) & gdn._lib.GDN_DEVERR_BAD_SEQLENS
+
+
+# ----------------------------------------------------------------------------- chunked tensor-core path
+@pytest.mark.parametrize("lens", [[63], [127, 128, 129], [256, 0, 1, 191], [1000]])
+def test_chunked_matches_oracle_at_chunk_boundaries(gdn, lens):
+    inp = gdn.workloads.prefill_inputs(lens, seed=40 + len(lens))
+    out, ns = gdn.kernel_prefill.run(**to_dev(inp))
+    o_ref, s_ref = oracle_prefill(inp, impl=c_oracle)
+    assert_match(out, ns, o_ref, s_ref)
+    assert gdn._lib.device_error() == 0
+
+
+def test_chunked_long_memory_gates(gdn):
+    """Decays close to 1 (long memory): the chunked path's bf16 operand splits must
+    keep the final state within tolerance over many chunks."""
+    inp = gdn.workloads.prefill_inputs([700, 1500], seed=41)
+    inp["dt_bias"] = inp["dt_bias"] - 6.0   # softplus(a + dt) ~ 1e-3  ->  g ~ 0.99
+    inp["A_log"] = inp["A_log"] * 0.2
+    out, ns = gdn.kernel_prefill.run(**to_dev(inp))
+    o_ref, s_ref = oracle_prefill(inp, impl=c_oracle)
+    assert_match(out, ns, o_ref, s_ref)
+
+
+def test_chunked_equals_serial_kernel(gdn):
+    inp = to_dev(gdn.workloads.prefill_inputs([300, 64, 5, 0, 77], seed=42))
+    o1, s1 = gdn.kernel_prefill.run(**inp)
+    o2, s2 = gdn.kernel_prefill.run(**inp, serial=True)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(o1.float().cpu().numpy(), o2.float().cpu().numpy(), **OUT_TOL)
+    ok, err = state_close(s1.cpu().numpy(), s2.cpu().numpy(), STATE_RTOL)
+    assert ok, err
