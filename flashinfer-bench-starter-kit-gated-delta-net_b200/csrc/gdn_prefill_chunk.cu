@@ -26,9 +26,12 @@
 //               Q scaled by G in place, blocked fp32 inverse T, T hi/lo and P tiles
 //   warp 12     TMA producer (K, Q: 128B-swizzled tiles, double-buffered; V plain)
 //   warp 13     TMEM allocator and MMA issuer
-// Hand-offs are mbarriers; every wait is bounded (kWaitLimitNs): a timeout
-// raises GDN_DEVERR_WAIT_TIMEOUT and an in-CTA abort flag so every role leaves
-// its loop, then in-flight copies and MMAs are drained before TMEM is freed.
+// Per chunk the state chain is S0 tiles -> [S0 [K;Qg]^T] -> R -> [R^T T^T] ->
+// deltas -> [S += Dt^T K] -> next chunk; the output MMA (D^T P^T), the output
+// stores and all prep work overlap it.  Hand-offs are mbarriers; every wait is
+// bounded (kWaitLimitNs): a timeout raises GDN_DEVERR_WAIT_TIMEOUT and an
+// in-CTA abort flag so every role leaves its loop, then in-flight copies and
+// MMAs are drained before TMEM is freed.
 #include <cuda.h>
 
 #include "gdn_common.cuh"
@@ -44,13 +47,13 @@ constexpr int kChainThreads = 256;
 constexpr int kWarpTma = 12, kWarpMma = 13;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
 // TMEM column map (fp32 accumulators; lanes = state row v unless noted)
 constexpr uint32_t kTmS = 0;     // [0,128)    state S[v][k]
-constexpr uint32_t kTmD1 = 128;  // [128,192)  S0 K^T
-constexpr uint32_t kTmD0 = 192;  // [192,256), [256,320): K K^T / Q K^T (lanes = token), stage s
-constexpr uint32_t kTmD2 = 320;  // [320,384)  D^T
-constexpr uint32_t kTmD3 = 384;  // [384,448)  O^T (unscaled)
+constexpr uint32_t kTmD1 = 128;  // 2 buffers [128,256), [256,384): cols 0-63 S0 K^T, 64-127 O^T (unscaled)
+constexpr uint32_t kTmD0 = 384;  // [384,448)  K K^T / Q K^T (lanes = token)
+constexpr uint32_t kTmD2 = 448;  // [448,512)  D^T
 
 // Shared-memory map (offsets from a 1024-byte aligned base)
 constexpr uint32_t kSmKQ = 0;          // 2 stages x 32 KB: [tile d0-63 | tile d64-127], rows 0-63 K, 64-127 Q
@@ -68,11 +71,11 @@ constexpr uint32_t kSmTs = 205824;     // T row-major [64][68] fp32
 constexpr uint32_t kSmGate = 223232;   // 2 stages x 6 arrays x 64 fp32
 constexpr uint32_t kSmBar = 226304;    // mbarriers (32 x 8 B)
 constexpr uint32_t kSmMisc = 226560;   // tmem base slot, abort flag
-constexpr uint32_t kSmX = 226624;      // solve block products [3][16][16] fp32
-constexpr uint32_t kSmBytes = 229696;
+constexpr uint32_t kSmX = 226624;      // solve: 32x32 block product X fp32 (4 KB)
+constexpr uint32_t kSmBytes = 230720;
 constexpr uint32_t kSmAlloc = kSmBytes + 1024;  // + alignment slack
 static_assert(kSmAs + 64 * kLd * 4 <= kSmTs && kSmTs + 64 * kLd * 4 <= kSmGate, "smem map");
-static_assert(kSmX + 3 * 256 * 4 <= kSmBytes, "smem map");
+static_assert(kSmX + 32 * 32 * 4 <= kSmBytes, "smem map");
 static_assert(kSmAlloc <= 232448, "smem budget");
 
 // gate arrays (per stage): log2-scaled prefix, beta, G, beta*G, exp(g_C - g), scratch
@@ -81,9 +84,12 @@ enum : int { GA_G2 = 0, GA_BETA = 1, GA_G = 2, GA_BG = 3, GA_R = 4, GA_TMP = 5, 
 enum : int {
   B_KQ_FULL = 0,   // [2]
   B_KQ_EMPTY = 2,  // [2]
-  B_KKQK = 4,      // [2]
-  B_GATES = 6,     // [2]
-  B_V_FULL = 8,
+  B_GATES = 4,     // [2]
+  B_GFREE = 6,     // [2] the chain is done with a gate stage (per stage, so a wait can never alias)
+  B_KKQK = 8,
+  B_D0_FREE,
+  B_QG_READY,
+  B_V_FULL,
   B_V_EMPTY,
   B_S0_READY,
   B_MMA1,
@@ -116,13 +122,13 @@ __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sy
 // Bounded wait that also gives up as soon as another role has aborted.
 __device__ __forceinline__ bool wait_bar(const Smem& sm, uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
-#pragma unroll 1
-  for (int i = 0; i < 1024; ++i)
-    if (mbar_try_wait(addr, parity)) return true;
+  if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait(addr, parity)) return true;
+    // suspended until the phase completes (or 0.1 ms), so waiting threads do not
+    // take issue slots from the warps doing the work
+    if (mbar_try_wait_sleep(addr, parity, 100000u)) return true;
     if (*sm.abort_flag()) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       raise_device_error(kDevErrWaitTimeout);
@@ -180,75 +186,77 @@ __device__ __forceinline__ void fma4(float4& acc, float a, const float4& t) {
 }
 
 // ---------------------------------------------------------------------------
-// Inverse of the unit lower-triangular 64x64 matrix I + A in fp32 by the prep
-// warpgroup (128 threads).  As = A row-major (stride kLd, zero on and above the
-// diagonal); the inverse is written to Ts (row-major, stride kLd; entries above
-// the diagonal blocks are left unwritten).
-//   1. diagonal 16x16 blocks, one column per thread (x_r = d_rc - sum_{q<r} A_rq x_q)
-//   2. T_ij = -T_ii X_ij, X_ij = sum_{k=j}^{i-1} A_ik T_kj, by block distance 1, 2, 3;
-//      each thread computes 1 x 4 output strips from float4 shared-memory loads.
-__device__ void solve_unit_lower(const float* As, float* Ts, float* Xs, int p) {
-  if (p < 64) {
-    const int o = (p >> 4) * 16, c = p & 15;
-    float x[16];
+// Inverse T of the unit lower-triangular 64x64 matrix I + A in fp32 (prep
+// warpgroup).  As = A row-major (stride kLd, zero on and above the diagonal);
+// T is written row-major to Ts (stride kLd; blocks above the diagonal blocks
+// are left unwritten).
+//   solve_diag16:  the four 16x16 diagonal blocks, one column per thread (64
+//                  threads): x_r = d_rc - sum_{q<r} A_rq x_q
+//   solve_merge:   for block pairs of size B (16, then 32): T_10 = -T_11 (A_10 T_00),
+//                  two products over the 128 threads in 1x4 strips, skipping the
+//                  zero triangles of T_00 and T_11; Xs holds A_10 T_00.
+__device__ __forceinline__ void solve_diag16(const float* As, float* Ts, int p) {
+  const int o = (p >> 4) * 16, c = p & 15;
+  float x[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      const float* arow = As + (o + r) * kLd + o;
-      float s0 = 0.f, s1 = 0.f;
+  for (int r = 0; r < 16; ++r) {
+    const float* arow = As + (o + r) * kLd + o;
+    float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int q4 = 0; q4 < r; q4 += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(arow + q4);
-        s0 = fmaf(a.x, x[q4], s0);
-        if (q4 + 1 < r) s1 = fmaf(a.y, x[q4 + 1], s1);
-        if (q4 + 2 < r) s0 = fmaf(a.z, x[q4 + 2], s0);
-        if (q4 + 3 < r) s1 = fmaf(a.w, x[q4 + 3], s1);
-      }
-      x[r] = (r == c ? 1.f : 0.f) - (s0 + s1);
+    for (int q4 = 0; q4 < r; q4 += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(arow + q4);
+      s0 = fmaf(a.x, x[q4], s0);
+      if (q4 + 1 < r) s1 = fmaf(a.y, x[q4 + 1], s1);
+      if (q4 + 2 < r) s0 = fmaf(a.z, x[q4 + 2], s0);
+      if (q4 + 3 < r) s1 = fmaf(a.w, x[q4 + 3], s1);
     }
+    x[r] = (r == c ? 1.f : 0.f) - (s0 + s1);
+  }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) Ts[(o + r) * kLd + o + c] = x[r];
+  for (int r = 0; r < 16; ++r) Ts[(o + r) * kLd + o + c] = x[r];
+}
+
+// lgB = log2(B); pairs are (rows/cols) [2mB, 2mB+B) (block 0) and [2mB+B, 2mB+2B) (block 1).
+__device__ __noinline__ void solve_merge(const float* As, float* Ts, float* Xs, int p, int lgB) {
+  const int B = 1 << lgB, lgQ = lgB - 2, items = 8 * B;  // (64 / 2B pairs) x B rows x B/4 quads
+  // X = A_10 T_00   (T_00[k][c] = 0 for k < c)
+#pragma unroll 1
+  for (int it = p; it < items; it += 128) {
+    const int m = it >> (lgB + lgQ), r = (it >> lgQ) & (B - 1), cq = it & ((B >> 2) - 1);
+    const int jo = 2 * m * B, io = jo + B;
+    const float* arow = As + (io + r) * kLd + jo;
+    const float* tcol = Ts + jo * kLd + jo + 4 * cq;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+    for (int kk = 4 * cq; kk < B; kk += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(arow + kk);
+      fma4(acc, a.x, *reinterpret_cast<const float4*>(tcol + (kk + 0) * kLd));
+      fma4(acc, a.y, *reinterpret_cast<const float4*>(tcol + (kk + 1) * kLd));
+      fma4(acc, a.z, *reinterpret_cast<const float4*>(tcol + (kk + 2) * kLd));
+      fma4(acc, a.w, *reinterpret_cast<const float4*>(tcol + (kk + 3) * kLd));
+    }
+    *reinterpret_cast<float4*>(Xs + ((m * B + r) << lgB) + 4 * cq) = acc;
   }
   named_sync(2, 128);
+  // T_10 = -T_11 X   (T_11[r][q] = 0 for q > r)
 #pragma unroll 1
-  for (int d = 1; d <= 3; ++d) {
-    const int items = (4 - d) * 64;  // (block, row r, column quad cq)
+  for (int it = p; it < items; it += 128) {
+    const int m = it >> (lgB + lgQ), r = (it >> lgQ) & (B - 1), cq = it & ((B >> 2) - 1);
+    const int jo = 2 * m * B, io = jo + B;
+    const float* trow = Ts + (io + r) * kLd + io;
+    const float* xb = Xs + ((m * B) << lgB) + 4 * cq;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-    for (int it = p; it < items; it += 128) {
-      const int blk = it >> 6, r = (it >> 2) & 15, cq = it & 3;
-      const int j = blk, i = blk + d;
-      const float* arow = As + (16 * i + r) * kLd;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-      for (int kk = 16 * j; kk < 16 * i; kk += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(arow + kk);
-        fma4(acc, a.x, *reinterpret_cast<const float4*>(Ts + (kk + 0) * kLd + 16 * j + 4 * cq));
-        fma4(acc, a.y, *reinterpret_cast<const float4*>(Ts + (kk + 1) * kLd + 16 * j + 4 * cq));
-        fma4(acc, a.z, *reinterpret_cast<const float4*>(Ts + (kk + 2) * kLd + 16 * j + 4 * cq));
-        fma4(acc, a.w, *reinterpret_cast<const float4*>(Ts + (kk + 3) * kLd + 16 * j + 4 * cq));
-      }
-      *reinterpret_cast<float4*>(Xs + blk * 256 + r * 16 + 4 * cq) = acc;
+    for (int q4 = 0; q4 <= r; q4 += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(trow + q4);
+      fma4(acc, a.x, *reinterpret_cast<const float4*>(xb + ((q4 + 0) << lgB)));
+      fma4(acc, a.y, *reinterpret_cast<const float4*>(xb + ((q4 + 1) << lgB)));
+      fma4(acc, a.z, *reinterpret_cast<const float4*>(xb + ((q4 + 2) << lgB)));
+      fma4(acc, a.w, *reinterpret_cast<const float4*>(xb + ((q4 + 3) << lgB)));
     }
-    named_sync(2, 128);
-#pragma unroll 1
-    for (int it = p; it < items; it += 128) {
-      const int blk = it >> 6, r = (it >> 2) & 15, cq = it & 3;
-      const int j = blk, i = blk + d;
-      const float* trow = Ts + (16 * i + r) * kLd + 16 * i;
-      const float* xb = Xs + blk * 256 + 4 * cq;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int q4 = 0; q4 < 16; q4 += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(trow + q4);
-        fma4(acc, a.x, *reinterpret_cast<const float4*>(xb + (q4 + 0) * 16));
-        fma4(acc, a.y, *reinterpret_cast<const float4*>(xb + (q4 + 1) * 16));
-        fma4(acc, a.z, *reinterpret_cast<const float4*>(xb + (q4 + 2) * 16));
-        fma4(acc, a.w, *reinterpret_cast<const float4*>(xb + (q4 + 3) * 16));
-      }
-      *reinterpret_cast<float4*>(Ts + (16 * i + r) * kLd + 16 * j + 4 * cq) =
-          make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
-    }
-    named_sync(2, 128);
+    *reinterpret_cast<float4*>(Ts + (io + r) * kLd + jo + 4 * cq) = make_float4(-acc.x, -acc.y, -acc.z, -acc.w);
   }
+  named_sync(2, 128);
 }
 
 // ---------------------------------------------------------------------------
@@ -317,37 +325,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ======================================================================= MMA issuer
   else if (warp == kWarpMma) {
     if (lane == 0 && nchunks > 0) {
+      using tc::kmajor_step;
+      using tc::mnmajor_step;
       const uint32_t id_n64 = tc::idesc_bf16(128, 64, false, false);
+      const uint32_t id_n128 = tc::idesc_bf16(128, 128, false, false);
       const uint32_t id_st = tc::idesc_bf16(128, 128, false, true);  // Dt^T x K (K MN-major)
-      const uint32_t aS0 = sm.addr(kSmS0), aRD = sm.addr(kSmRD), aDt = sm.addr(kSmDt);
-      const uint32_t aT = sm.addr(kSmT), aP = sm.addr(kSmP);
+      // descriptor bases (start address of each operand buffer); per MMA step only a
+      // constant is added (tc::kmajor_step / tc::mnmajor_step)
+      const uint64_t dS0 = tc::kmajor_desc(sm.addr(kSmS0), 0, 0);
+      const uint64_t dRD = tc::kmajor_desc(sm.addr(kSmRD), 0, 0);
+      const uint64_t dRDlo = tc::kmajor_desc(sm.addr(kSmRD + 16384), 0, 0);
+      const uint64_t dDt = tc::kmajor_desc(sm.addr(kSmDt), 0, 0);
+      const uint64_t dT = tc::kmajor_desc(sm.addr(kSmT), 0, 0);
+      const uint64_t dTlo = tc::kmajor_desc(sm.addr(kSmT + 8192), 0, 0);
+      const uint64_t dP = tc::kmajor_desc(sm.addr(kSmP), 0, 0);
+      const uint64_t dKQ0 = tc::kmajor_desc(sm.addr(kSmKQ), 0, 0);
+      const uint64_t dKQ1 = tc::kmajor_desc(sm.addr(kSmKQ + kKQStage), 0, 0);
+      const uint64_t dKmn0 = tc::mnmajor_desc(sm.addr(kSmKQ), kKQTile, 0);
+      const uint64_t dKmn1 = tc::mnmajor_desc(sm.addr(kSmKQ + kKQStage), kKQTile, 0);
       auto issue_kkqk = [&](int i) -> bool {
         const int s = i & 1;
         if (!wait_bar(sm, sm.bar(B_KQ_FULL + s), (i >> 1) & 1)) return false;
+        if (i >= 1 && !wait_bar(sm, sm.bar(B_D0_FREE), (i - 1) & 1)) return false;
         tc::fence_after_sync();
-        const uint32_t kq = sm.addr(kSmKQ + s * kKQStage);
-#pragma unroll
+        const uint64_t d = s ? dKQ1 : dKQ0;
+#pragma unroll 1
         for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(tmem + kTmD0 + s * 64, tc::kmajor_desc(kq, kKQTile, ks), tc::kmajor_desc(kq, kKQTile, ks),
-                       id_n64, ks > 0);
-        tc::mma_commit(sm.bar(B_KKQK + s));
+          tc::mma_bf16(tmem + kTmD0, d + kmajor_step(kKQTile, ks), d + kmajor_step(kKQTile, ks), id_n64, ks > 0);
+        tc::mma_commit(sm.bar(B_KKQK));
         return true;
       };
       bool ok = issue_kkqk(0);
       for (int i = 0; ok && i < nchunks; ++i) {
         const int s = i & 1;
-        const uint32_t kq = sm.addr(kSmKQ + s * kKQStage);
-        // MMA1: D1 = S0_hi K^T + S0_lo K^T
+        const uint64_t dK = s ? dKQ1 : dKQ0;
+        const uint64_t dKmn = s ? dKmn1 : dKmn0;
+        const uint32_t d1 = tmem + kTmD1 + (uint32_t)s * 128;
+        // MMA1: D1 = S0_hi [K; Qg]^T (N = 128), then D1[:, K part] += S0_lo K^T
         if (!wait_bar(sm, sm.bar(B_S0_READY), i & 1)) break;
+        if (!wait_bar(sm, sm.bar(B_QG_READY), i & 1)) break;
+        if (i >= 2 && !wait_bar(sm, sm.bar(B_OUT_DONE), i & 1)) break;  // outputs of chunk i-2 read D1[s]
         tc::fence_after_sync();
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(tmem + kTmD1, tc::kmajor_desc(aS0, kKQTile, ks), tc::kmajor_desc(kq, kKQTile, ks), id_n64,
-                       ks > 0);
-#pragma unroll
+          tc::mma_bf16(d1, dS0 + kmajor_step(kKQTile, ks), dK + kmajor_step(kKQTile, ks), id_n128, ks > 0);
+#pragma unroll 1
         for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(tmem + kTmD1, tc::kmajor_desc(aRD, kKQTile, ks), tc::kmajor_desc(kq, kKQTile, ks), id_n64,
-                       true);
+          tc::mma_bf16(d1, dRD + kmajor_step(kKQTile, ks), dK + kmajor_step(kKQTile, ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA1));
         // next chunk's K K^T / Q K^T
         if (i + 1 < nchunks && !issue_kkqk(i + 1)) break;
@@ -355,36 +379,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_bar(sm, sm.bar(B_R_READY), i & 1)) break;
         if (!wait_bar(sm, sm.bar(B_PREP_DONE), i & 1)) break;
         tc::fence_after_sync();
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tmem + kTmD2, tc::kmajor_desc(aRD, 0, ks), tc::kmajor_desc(aT, 0, ks), id_n64, ks > 0);
-#pragma unroll
+          tc::mma_bf16(tmem + kTmD2, dRD + kmajor_step(0, ks), dT + kmajor_step(0, ks), id_n64, ks > 0);
+#pragma unroll 1
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tmem + kTmD2, tc::kmajor_desc(aRD + 16384, 0, ks), tc::kmajor_desc(aT, 0, ks), id_n64, true);
-#pragma unroll
+          tc::mma_bf16(tmem + kTmD2, dRDlo + kmajor_step(0, ks), dT + kmajor_step(0, ks), id_n64, true);
+#pragma unroll 1
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tmem + kTmD2, tc::kmajor_desc(aRD, 0, ks), tc::kmajor_desc(aT + 8192, 0, ks), id_n64, true);
+          tc::mma_bf16(tmem + kTmD2, dRD + kmajor_step(0, ks), dTlo + kmajor_step(0, ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA2));
-        // O^T = S0_hi Qg^T + D^T P^T;   S += Dt^T K (hi/lo)
+        // state first: S += Dt^T K (hi/lo); then the output: D1[:, O part] += D^T P^T
         if (!wait_bar(sm, sm.bar(B_D_READY), i & 1)) break;
         tc::fence_after_sync();
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(tmem + kTmD3, tc::kmajor_desc(aS0, kKQTile, ks), tc::kmajor_desc(kq + 8192, kKQTile, ks),
-                       id_n64, ks > 0);
-#pragma unroll
+#pragma unroll 1
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tmem + kTmD3, tc::kmajor_desc(aDt, 0, ks), tc::kmajor_desc(aP, 0, ks), id_n64, true);
-        tc::mma_commit(sm.bar(B_MMA3));
-#pragma unroll
+          tc::mma_bf16(tmem + kTmS, dRD + kmajor_step(0, ks), dKmn + mnmajor_step(ks), id_st, true);
+#pragma unroll 1
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tmem + kTmS, tc::kmajor_desc(aRD, 0, ks), tc::mnmajor_desc(kq, kKQTile, ks), id_st, true);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(tmem + kTmS, tc::kmajor_desc(aRD + 16384, 0, ks), tc::mnmajor_desc(kq, kKQTile, ks), id_st,
-                       true);
+          tc::mma_bf16(tmem + kTmS, dRDlo + kmajor_step(0, ks), dKmn + mnmajor_step(ks), id_st, true);
         tc::mma_commit(sm.bar(B_MMA4));
         tc::mma_commit(sm.bar(B_KQ_EMPTY + s));
+#pragma unroll 1
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_bf16(d1 + 64, dDt + kmajor_step(0, ks), dP + kmajor_step(0, ks), id_n64, true);
+        tc::mma_commit(sm.bar(B_MMA3));
       }
       // drain: every MMA issued above has completed before TMEM is released
       tc::mma_commit(sm.bar(B_DRAIN));
@@ -398,28 +417,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* As = sm.As();
     float* Ts = sm.Ts();
     const float A_log = p.A_log[h], dt_bias = p.dt_bias[h];
-    // gate inputs, loaded one chunk ahead
-    float a_nx = 0.f, b_nx = 0.f;
+    const float eA = tc::ex2_approx(A_log * kLog2e);
+    // gate inputs (raw bf16 bits), loaded one chunk ahead and converted at use so
+    // the load latency is not paid where they are issued
+    unsigned short a_nx = 0, b_nx = 0;
     auto load_ab = [&](int i) {
       if (pth < 64 && (int64_t)i * kC + pth < len) {
         const int64_t tok = t0 + (int64_t)i * kC + pth;
-        a_nx = bf16_to_f32(p.a + tok * p.a_st + h);
-        b_nx = bf16_to_f32(p.b + tok * p.b_st + h);
+        a_nx = reinterpret_cast<const unsigned short*>(p.a)[tok * p.a_st + h];
+        b_nx = reinterpret_cast<const unsigned short*>(p.b)[tok * p.b_st + h];
       }
     };
     if (nchunks > 0) load_ab(0);
     for (int i = 0; i < nchunks; ++i) {
       const int s = i & 1;
-      // ---- gates of chunk i into stage s (free once the chain finished chunk i-2) ----
-      const float a_cur = a_nx, b_cur = b_nx;
+      // ---- gates of chunk i into stage s (free once the chain's deltas of chunk i-2 are done) ----
+      const float a_cur = __uint_as_float((uint32_t)a_nx << 16), b_cur = __uint_as_float((uint32_t)b_nx << 16);
       if (i + 1 < nchunks) load_ab(i + 1);
-      if (i >= 2 && !group_wait(sm, B_OUT_DONE, (i - 2) & 1, 2, 128, pth == 0)) break;
+      if (i >= 2 && !group_wait(sm, B_GFREE + s, ((i - 2) >> 1) & 1, 2, 128, pth == 0)) break;
       if (pth < 64) {
+        // g = exp(-exp(A_log) softplus(a + dt_bias)), softplus(x) = x for x > 20 else log(1 + e^x);
+        // beta = sigmoid(b)  (kernel_prefill.py:108-113), with the hardware exp2/log2
         const bool valid = (int64_t)i * kC + pth < len;
         float lg = 0.f, bt = 0.f;
         if (valid) {
-          lg = gdn_log_decay(A_log, a_cur, dt_bias);
-          bt = 1.0f / (1.0f + expf(-b_cur));
+          const float x = a_cur + dt_bias;
+          const float sp = x > 20.f ? x : kLn2 * tc::lg2_approx(1.f + tc::ex2_approx(x * kLog2e));
+          lg = -eA * sp;
+          bt = 1.f / (1.f + tc::ex2_approx(-b_cur * kLog2e));
         }
         float x = lg;  // inclusive scan over the 64 tokens: warp scans + carry
 #pragma unroll
@@ -433,81 +458,90 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (pth >= 32) x += tmp[0];
         if (pth == 63) tmp[1] = x;
         named_sync(3, 64);
-        const float gC = tmp[1];
-        const float G = expf(x);
-        sm.gate(s, GA_G2)[pth] = x * kLog2e;
+        const float x2 = x * kLog2e, gC2 = tmp[1] * kLog2e;
+        const float G = tc::ex2_approx(x2);
+        sm.gate(s, GA_G2)[pth] = x2;
         sm.gate(s, GA_BETA)[pth] = bt;
         sm.gate(s, GA_G)[pth] = G;
         sm.gate(s, GA_BG)[pth] = bt * G;
-        sm.gate(s, GA_R)[pth] = expf(gC - x);
+        sm.gate(s, GA_R)[pth] = tc::ex2_approx(gC2 - x2);
       }
       named_sync(2, 128);
       if (pth == 0) mbar_arrive(sm.bar(B_GATES + s));
       // ---- A (row-major fp32) and P (registers) from K K^T / Q K^T ----
-      if (!group_wait(sm, B_KKQK + s, (i >> 1) & 1, 2, 128, pth == 0)) break;
+      if (!group_wait(sm, B_KKQK, i & 1, 2, 128, pth == 0)) break;
       tc::fence_after_sync();
       const float* g2 = sm.gate(s, GA_G2);
       uint32_t prow[32];
       {
-        float v[32];
         const float gt = g2[row];
-        const float bt = sm.gate(s, GA_BETA)[row];
+        const uint32_t d0 = tc::tmem_addr(tmem, (uint32_t)((warp & 3) * 32), kTmD0);
+        if (pth < 64) {  // A row (warps 8, 9): rolled loop
+          const float bt = sm.gate(s, GA_BETA)[row];
+#pragma unroll 1
+          for (int j8 = 0; j8 < 8; ++j8) {
+            float v[8];
+            tc::tmem_ld8(d0 + j8 * 8, v);
+            const float4 g0 = *reinterpret_cast<const float4*>(g2 + j8 * 8);
+            const float4 g1 = *reinterpret_cast<const float4*>(g2 + j8 * 8 + 4);
+            tc::tmem_wait_ld();
+            const float gj[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            float w[8];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tc::tmem_ld32(tc::tmem_addr(tmem, (uint32_t)((warp & 3) * 32), kTmD0 + s * 64 + half * 32), v);
-          tc::tmem_wait_ld();
-          if (pth < 64) {
+            for (int u = 0; u < 8; ++u) w[u] = j8 * 8 + u < row ? bt * tc::ex2_approx(gt - gj[u]) * v[u] : 0.f;
+            *reinterpret_cast<float4*>(As + row * kLd + j8 * 8) = make_float4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<float4*>(As + row * kLd + j8 * 8 + 4) = make_float4(w[4], w[5], w[6], w[7]);
+          }
+        } else {  // P row (warps 10, 11): kept in registers until the P tile is free
 #pragma unroll
-            for (int q = 0; q < 32; q += 4) {
-              const int j = half * 32 + q;
-              const float4 gj = *reinterpret_cast<const float4*>(g2 + j);
-              float4 w;
-              w.x = j < row ? bt * tc::ex2_approx(gt - gj.x) * v[q] : 0.f;
-              w.y = j + 1 < row ? bt * tc::ex2_approx(gt - gj.y) * v[q + 1] : 0.f;
-              w.z = j + 2 < row ? bt * tc::ex2_approx(gt - gj.z) * v[q + 2] : 0.f;
-              w.w = j + 3 < row ? bt * tc::ex2_approx(gt - gj.w) * v[q + 3] : 0.f;
-              *reinterpret_cast<float4*>(As + row * kLd + j) = w;
-            }
-          } else {
+          for (int j8 = 0; j8 < 8; ++j8) {
+            float v[8];
+            tc::tmem_ld8(d0 + j8 * 8, v);
+            const float4 g0 = *reinterpret_cast<const float4*>(g2 + j8 * 8);
+            const float4 g1 = *reinterpret_cast<const float4*>(g2 + j8 * 8 + 4);
+            tc::tmem_wait_ld();
+            const float gj[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+            float w[8];
 #pragma unroll
-            for (int q = 0; q < 32; q += 4) {
-              const int j = half * 32 + q;
-              const float4 gj = *reinterpret_cast<const float4*>(g2 + j);
-              const float p0 = j <= row ? tc::ex2_approx(gt - gj.x) * v[q] : 0.f;
-              const float p1 = j + 1 <= row ? tc::ex2_approx(gt - gj.y) * v[q + 1] : 0.f;
-              const float p2 = j + 2 <= row ? tc::ex2_approx(gt - gj.z) * v[q + 2] : 0.f;
-              const float p3 = j + 3 <= row ? tc::ex2_approx(gt - gj.w) * v[q + 3] : 0.f;
-              prow[(half * 32 + q) >> 1] = pack_bf16x2(p0, p1);
-              prow[((half * 32 + q) >> 1) + 1] = pack_bf16x2(p2, p3);
-            }
+            for (int u = 0; u < 8; ++u) w[u] = j8 * 8 + u <= row ? tc::ex2_approx(gt - gj[u]) * v[u] : 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) prow[j8 * 4 + u] = pack_bf16x2(w[2 * u], w[2 * u + 1]);
           }
         }
       }
       tc::fence_before_sync();
-      // ---- Q rows of the K/Q stage scaled by G in place (Qg for the output MMA) ----
-      {
+      named_sync(2, 128);  // A complete, D0 read
+      if (pth == 0) mbar_arrive(sm.bar(B_D0_FREE));
+      // ---- diagonal 16x16 blocks of T on threads 0-63, while threads 64-127 scale the
+      //      Q rows of the K/Q stage by G in place (Qg for the first MMA of chunk i) ----
+      if (pth < 64) {
+        solve_diag16(As, Ts, pth);
+      } else {
         const float Gt = sm.gate(s, GA_G)[row];
-        unsigned char* qtile = sm.base + kSmKQ + s * kKQStage + (pth >> 6) * kKQTile;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          const uint32_t off = tc::sw128_offset(64 + row, c8 * 8);
-          uint4 w = *reinterpret_cast<const uint4*>(qtile + off);
+        unsigned char* qstage = sm.base + kSmKQ + s * kKQStage;
+#pragma unroll 2
+        for (int c16 = 0; c16 < 16; ++c16) {
+          const uint32_t off = (uint32_t)(c16 >> 3) * kKQTile + tc::sw128_offset(64 + row, (c16 & 7) * 8);
+          uint4 w = *reinterpret_cast<const uint4*>(qstage + off);
           w.x = pack_bf16x2(__uint_as_float(w.x << 16) * Gt, __uint_as_float(w.x & 0xffff0000u) * Gt);
           w.y = pack_bf16x2(__uint_as_float(w.y << 16) * Gt, __uint_as_float(w.y & 0xffff0000u) * Gt);
           w.z = pack_bf16x2(__uint_as_float(w.z << 16) * Gt, __uint_as_float(w.z & 0xffff0000u) * Gt);
           w.w = pack_bf16x2(__uint_as_float(w.w << 16) * Gt, __uint_as_float(w.w & 0xffff0000u) * Gt);
-          *reinterpret_cast<uint4*>(qtile + off) = w;
+          *reinterpret_cast<uint4*>(qstage + off) = w;
         }
+        tc::fence_proxy_async_smem();
       }
       named_sync(2, 128);
-      // ---- T = (I + A)^-1 ----
-      solve_unit_lower(As, Ts, sm.Xs(), pth);
+      if (pth == 0) mbar_arrive(sm.bar(B_QG_READY));
+      // ---- T = (I + A)^-1: off-diagonal blocks, 16 -> 32 -> 64 ----
+      solve_merge(As, Ts, sm.Xs(), pth, 4);
+      solve_merge(As, Ts, sm.Xs(), pth, 5);
       // ---- T hi/lo tiles (after MMA2 of chunk i-1), P tile (after MMA3 of chunk i-1) ----
       if (i >= 1 && !group_wait(sm, B_MMA2, (i - 1) & 1, 2, 128, pth == 0)) break;
       if (pth < 64) {
         unsigned char* thi = sm.base + kSmT;
         unsigned char* tlo = sm.base + kSmT + 8192;
-#pragma unroll
+#pragma unroll 1
         for (int c8 = 0; c8 < 8; ++c8) {
           const float4 x0 = *reinterpret_cast<const float4*>(Ts + pth * kLd + c8 * 8);
           const float4 x1 = *reinterpret_cast<const float4*>(Ts + pth * kLd + c8 * 8 + 4);
@@ -568,39 +602,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* dtt = sm.base + kSmDt;
     const __nv_bfloat16* vt = reinterpret_cast<const __nv_bfloat16*>(sm.base + kSmV);
     const int tb = hsel * 32;  // this thread's token columns [tb, tb + 32)
+    // outputs of chunk ci: o[t][v] = scale * O^T[v][t] (D1 buffer ci & 1, columns 64-127);
+    // lane pairs exchange so each stores bf16x2.  Requires MMA3(ci) complete.
+    auto emit_out = [&](int ci) {
+      const int64_t rem = len - (int64_t)ci * kC;
+      const int nvalid = rem < kC ? (int)rem : kC;
+      const bool odd = lane & 1;
+      const int vcol = v & ~1;
+      __nv_bfloat16* out = p.out + (t0 + (int64_t)ci * kC) * p.o_st + (int64_t)h * p.o_sh + vcol;
+#pragma unroll 1
+      for (int c8 = 0; c8 < 4; ++c8) {
+        float x[8];
+        tc::tmem_ld8(tc::tmem_addr(tmem, lane_base, kTmD1 + (uint32_t)(ci & 1) * 128 + 64 + tb + c8 * 8), x);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 8; q += 2) {
+          // even lane keeps token q (needs the odd neighbour's column), odd lane keeps token q + 1
+          const float send = odd ? x[q] : x[q + 1];
+          const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+          const float c0v = odd ? recv : x[q];      // column vcol
+          const float c1v = odd ? x[q + 1] : recv;  // column vcol + 1
+          const int t = tb + c8 * 8 + q + (odd ? 1 : 0);
+          if (t < nvalid)
+            *reinterpret_cast<uint32_t*>(out + (int64_t)t * p.o_st) = pack_bf16x2(scale * c0v, scale * c1v);
+        }
+      }
+      tc::fence_before_sync();
+      named_sync(1, kChainThreads);
+      if (leader) mbar_arrive(sm.bar(B_OUT_DONE));
+    };
     for (int i = 0; i < nchunks; ++i) {
       const int s = i & 1;
-      const int64_t rem = len - (int64_t)i * kC;
-      const int nvalid = rem < kC ? (int)rem : kC;
       if (!group_wait(sm, B_GATES + s, (i >> 1) & 1, 1, kChainThreads, leader)) break;
       const float GC = sm.gate(s, GA_G)[63];
       // ---- S0 hi/lo tiles and S <- G_C * S (64 columns per thread) ----
       if (i > 0 && !group_wait(sm, B_MMA4, (i - 1) & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
-#pragma unroll
-      for (int c32 = 0; c32 < 2; ++c32) {
-        float x[32];
-        const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64 + c32 * 32);
-        tc::tmem_ld32(ta, x);
+#pragma unroll 2
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float x[8];
+        const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64 + c8 * 8);
+        tc::tmem_ld8(ta, x);
         tc::tmem_wait_ld();
+        uint4 hi, lo;
+        split2(x[0], x[1], hi.x, lo.x);
+        split2(x[2], x[3], hi.y, lo.y);
+        split2(x[4], x[5], hi.z, lo.z);
+        split2(x[6], x[7], hi.w, lo.w);
+        st_tile(s0t, v, c8, hi);
+        st_tile(s0l, v, c8, lo);
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          uint4 hi, lo;
-          split2(x[c8 * 8 + 0], x[c8 * 8 + 1], hi.x, lo.x);
-          split2(x[c8 * 8 + 2], x[c8 * 8 + 3], hi.y, lo.y);
-          split2(x[c8 * 8 + 4], x[c8 * 8 + 5], hi.z, lo.z);
-          split2(x[c8 * 8 + 6], x[c8 * 8 + 7], hi.w, lo.w);
-          st_tile(s0t, v, c32 * 4 + c8, hi);
-          st_tile(s0l, v, c32 * 4 + c8, lo);
-        }
-        float x0[16], x1[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          x0[q] = x[q] * GC;
-          x1[q] = x[16 + q] * GC;
-        }
-        tc::tmem_st16(ta, x0);
-        tc::tmem_st16(ta + 16, x1);
+        for (int q = 0; q < 8; ++q) x[q] *= GC;
+        tc::tmem_st8(ta, x);
       }
       tc::tmem_wait_st();
       tc::fence_proxy_async_smem();
@@ -608,30 +661,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_sync(1, kChainThreads);
       if (leader) mbar_arrive(sm.bar(B_S0_READY));
       // ---- R^T = beta V^T - beta G (S0 K^T), split hi/lo (32 token columns per thread) ----
-      if (!group_wait(sm, B_MMA1, i & 1, 1, kChainThreads, leader)) break;
       if (!group_wait(sm, B_V_FULL, i & 1, 1, kChainThreads, leader)) break;
+      if (!group_wait(sm, B_MMA1, i & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
       {
-        float x[32];
-        tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, kTmD1 + tb), x);
-        tc::tmem_wait_ld();
         const float* bet = sm.gate(s, GA_BETA) + tb;
         const float* bg = sm.gate(s, GA_BG) + tb;
-#pragma unroll
+#pragma unroll 2
         for (int c8 = 0; c8 < 4; ++c8) {
+          float x[8], vv[8];
+          tc::tmem_ld8(tc::tmem_addr(tmem, lane_base, kTmD1 + (uint32_t)s * 128 + tb + c8 * 8), x);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) vv[u] = __bfloat162float(vt[(tb + c8 * 8 + u) * kHeadDim + v]);
+          const float4 b0 = *reinterpret_cast<const float4*>(bet + c8 * 8);
+          const float4 b1 = *reinterpret_cast<const float4*>(bet + c8 * 8 + 4);
+          const float4 g0 = *reinterpret_cast<const float4*>(bg + c8 * 8);
+          const float4 g1 = *reinterpret_cast<const float4*>(bg + c8 * 8 + 4);
+          tc::tmem_wait_ld();
+          const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+          const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
           float r8[8];
 #pragma unroll
-          for (int q4 = 0; q4 < 8; q4 += 4) {
-            const float4 b4 = *reinterpret_cast<const float4*>(bet + c8 * 8 + q4);
-            const float4 g4 = *reinterpret_cast<const float4*>(bg + c8 * 8 + q4);
-            const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, gg[4] = {g4.x, g4.y, g4.z, g4.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int q = c8 * 8 + q4 + u;
-              const float vv = __bfloat162float(vt[(tb + q) * kHeadDim + v]);
-              r8[q4 + u] = fmaf(bb[u], vv, -gg[u] * x[q]);
-            }
-          }
+          for (int u = 0; u < 8; ++u) r8[u] = fmaf(bb[u], vv[u], -gg[u] * x[u]);
           uint4 hi, lo;
           split2(r8[0], r8[1], hi.x, lo.x);
           split2(r8[2], r8[3], hi.y, lo.y);
@@ -648,19 +699,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(sm.bar(B_R_READY));
         mbar_arrive(sm.bar(B_V_EMPTY));
       }
+      // ---- previous chunk's outputs, in the shadow of this chunk's second MMA ----
+      if (i > 0) {
+        if (!group_wait(sm, B_MMA3, (i - 1) & 1, 1, kChainThreads, leader)) break;
+        tc::fence_after_sync();
+        emit_out(i - 1);
+      }
       // ---- deltas: D^T (bf16, output MMA) and Dt^T = D^T exp(gC - g) (hi/lo, state MMA) ----
       if (!group_wait(sm, B_MMA2, i & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
       {
-        float x[32];
-        tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, kTmD2 + tb), x);
-        tc::tmem_wait_ld();
         const float* rr = sm.gate(s, GA_R) + tb;
-#pragma unroll
+#pragma unroll 2
         for (int c8 = 0; c8 < 4; ++c8) {
+          float d[8];
+          tc::tmem_ld8(tc::tmem_addr(tmem, lane_base, kTmD2 + tb + c8 * 8), d);
           const float4 r0 = *reinterpret_cast<const float4*>(rr + c8 * 8);
           const float4 r1 = *reinterpret_cast<const float4*>(rr + c8 * 8 + 4);
-          const float* d = x + c8 * 8;
+          tc::tmem_wait_ld();
           uint4 dd, hi, lo;
           dd.x = pack_bf16x2(d[0], d[1]);
           dd.y = pack_bf16x2(d[2], d[3]);
@@ -678,47 +734,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       named_sync(1, kChainThreads);
-      if (leader) mbar_arrive(sm.bar(B_D_READY));
-      // ---- outputs: o[t][v] = scale * O^T[v][t]; lane pairs exchange so each stores bf16x2 ----
-      if (!group_wait(sm, B_MMA3, i & 1, 1, kChainThreads, leader)) break;
-      tc::fence_after_sync();
-      {
-        float x[32];
-        tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, kTmD3 + tb), x);
-        tc::tmem_wait_ld();
-        const bool odd = lane & 1;
-        const int vcol = v & ~1;
-        __nv_bfloat16* out = p.out + (t0 + (int64_t)i * kC) * p.o_st + (int64_t)h * p.o_sh + vcol;
-#pragma unroll
-        for (int q = 0; q < 32; q += 2) {
-          // even lane keeps token q (needs the odd neighbour's column), odd lane keeps token q + 1
-          const float send = odd ? x[q] : x[q + 1];
-          const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-          const float c0v = odd ? recv : x[q];      // column vcol
-          const float c1v = odd ? x[q + 1] : recv;  // column vcol + 1
-          const int t = tb + q + (odd ? 1 : 0);
-          if (t < nvalid)
-            *reinterpret_cast<uint32_t*>(out + (int64_t)t * p.o_st) = pack_bf16x2(scale * c0v, scale * c1v);
-        }
+      if (leader) {
+        mbar_arrive(sm.bar(B_D_READY));
+        mbar_arrive(sm.bar(B_GFREE + s));
       }
-      tc::fence_before_sync();
-      named_sync(1, kChainThreads);
-      if (leader) mbar_arrive(sm.bar(B_OUT_DONE));
     }
-    // ---- final state ----
+    // ---- last chunk's outputs and the final state ----
     bool ok = true;
-    if (nchunks > 0) ok = group_wait(sm, B_MMA4, (nchunks - 1) & 1, 1, kChainThreads, leader) && !*sm.abort_flag();
+    if (nchunks > 0) {
+      ok = group_wait(sm, B_MMA4, (nchunks - 1) & 1, 1, kChainThreads, leader) &&
+           group_wait(sm, B_MMA3, (nchunks - 1) & 1, 1, kChainThreads, leader) && !*sm.abort_flag();
+      if (ok) {
+        tc::fence_after_sync();
+        emit_out(nchunks - 1);
+      }
+    }
     if (ok) {
       tc::fence_after_sync();
       float* dst = p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh + (size_t)v * kHeadDim + hsel * 64;
-#pragma unroll
-      for (int c32 = 0; c32 < 2; ++c32) {
-        float x[32];
-        tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64 + c32 * 32), x);
+#pragma unroll 1
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float x[8];
+        tc::tmem_ld8(tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64 + c8 * 8), x);
         tc::tmem_wait_ld();
-#pragma unroll
-        for (int q = 0; q < 32; q += 4)
-          *reinterpret_cast<float4*>(dst + c32 * 32 + q) = make_float4(x[q], x[q + 1], x[q + 2], x[q + 3]);
+        *reinterpret_cast<float4*>(dst + c8 * 8) = make_float4(x[0], x[1], x[2], x[3]);
+        *reinterpret_cast<float4*>(dst + c8 * 8 + 4) = make_float4(x[4], x[5], x[6], x[7]);
       }
     }
   }

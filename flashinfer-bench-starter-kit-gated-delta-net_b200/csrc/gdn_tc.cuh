@@ -60,6 +60,14 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile0, uint32_t mn_til
   return sdesc_sw128(tile0 + (uint32_t)k_step * 2048u, mn_tile_bytes, 1024u);
 }
 
+// Descriptor arithmetic for hot loops: the start-address field holds addr >> 4
+// in the low 14 bits and every shared-memory address here is below 256 KB, so
+// a descriptor for (tile0 + byte offset) is the tile0 descriptor plus offset >> 4.
+__host__ __device__ constexpr uint64_t kmajor_step(uint32_t tile_bytes, int k_step) {
+  return (uint64_t)(((uint32_t)(k_step >> 2) * tile_bytes + (uint32_t)(k_step & 3) * 32u) >> 4);
+}
+__host__ __device__ constexpr uint64_t mnmajor_step(int k_step) { return (uint64_t)((uint32_t)k_step * 128u); }
+
 // Byte offset of element (row, col) inside a SW128 tile of 64 bf16 columns.
 __device__ __forceinline__ uint32_t sw128_offset(int row, int col) {
   return (uint32_t)row * 128u + ((((uint32_t)col >> 3) ^ ((uint32_t)row & 7u)) << 4) + (((uint32_t)col & 7u) << 1);
@@ -99,6 +107,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 32 bit, 8 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+               : "memory");
+}
+
 // 32 lanes x 32 bit, 32 consecutive columns per thread.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -118,6 +144,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// log2(x) with the hardware's approximate base-2 logarithm (MUFU).
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
