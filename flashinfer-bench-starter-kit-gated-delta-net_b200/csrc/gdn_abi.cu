@@ -164,13 +164,12 @@ int gdn_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void
 
 size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_t num_qk_heads, int32_t num_v_heads,
                                   int32_t head_dim, uint32_t flags) {
-  (void)num_seqs;
-  (void)total_tokens;
   (void)num_qk_heads;
-  (void)num_v_heads;
   (void)head_dim;
-  (void)flags;
-  return 0;
+  // the token-serial kernel (forced, or for in-kernel q/k normalisation) needs none;
+  // the chunked kernel keeps one prepared record per chunk slot and v-head
+  if (flags & (GDN_FLAG_PREFILL_SERIAL | GDN_FLAG_QK_L2NORM)) return 0;
+  return gdn::prefill_chunk_workspace_bytes(num_seqs, total_tokens, num_v_heads);
 }
 
 int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,

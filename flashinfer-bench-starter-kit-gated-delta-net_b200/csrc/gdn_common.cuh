@@ -68,6 +68,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return done != 0;
 }
 
+// Non-blocking test of the phase with the given parity (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Same test, but the thread may be suspended (instead of spinning and taking
 // issue slots from working warps) until the phase completes or `hint_ns` passes.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity, uint32_t hint_ns) {
@@ -93,6 +106,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_device_error(kDevErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// Same bounded wait, but the thread is suspended between tests (for waits of a
+// microsecond or more, e.g. on a copy from HBM, where polling would only take
+// issue slots and shared-memory bandwidth from the warps doing the work).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  const unsigned long long t0 = globaltimer_ns();
+#pragma unroll 1
+  while (true) {
+    if (mbar_try_wait_sleep(addr, parity, 1000000u)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       raise_device_error(kDevErrWaitTimeout);
       return false;

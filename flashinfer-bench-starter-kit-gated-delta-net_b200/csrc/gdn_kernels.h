@@ -64,7 +64,9 @@ cudaError_t launch_decode(const DecodeParams& p, int rows, cudaStream_t stream);
 cudaError_t launch_prefill_serial(const PrefillParams& p, cudaStream_t stream);
 
 // Chunked tensor-core prefill: usable when q/k/v rows and strides are 16-byte
-// aligned (TMA) and no in-kernel q/k normalisation is requested.
+// aligned (TMA), no in-kernel q/k normalisation is requested and the workspace
+// holds prefill_chunk_workspace_bytes (one record per chunk slot and v-head).
+size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads);
 bool prefill_chunk_supported(const PrefillParams& p);
 cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream);
 

@@ -1,0 +1,97 @@
+// Pieces shared by the two kernels of the chunked prefill (sm_100a):
+//   prefill_prep_kernel   (gdn_prefill_prep.cu)   state-independent per-chunk
+//                         work for every chunk of every (sequence, v-head) at
+//                         once: gates, A, T = (I + A)^-1 and its bf16 split
+//   prefill_chunk_kernel  (gdn_prefill_chunk.cu)  the sequential state chain
+// They meet in the workspace: one record per (chunk slot, v-head).
+//
+// Chunk slots.  cu_seqlens lives on the device, so the host sizes the workspace
+// from (num_seqs, total_tokens) alone: chunk i of sequence n (tokens
+// [cu[n] + 64 i, min(cu[n] + 64 (i + 1), cu[n + 1]))) owns slot
+//   slot(n, i) = floor(cu[n] / 64) + n + i.
+// For monotone cu_seqlens the slots of different sequences never collide
+// (floor(c0/64) + ceil((c1-c0)/64) <= floor(c1/64) + 1) and every slot is
+// below total_tokens / 64 + num_seqs + 1.
+//
+// Record (kRecBytes, 16-byte aligned), written by the prep kernel and copied
+// verbatim into shared memory by the chain kernel's bulk copies:
+//   [0, 8192)      T hi: SW128 tile image [64 rows t][64 cols j] bf16, K-major
+//   [8192, 16384)  T lo: same, T - hi
+//   [16384, 17664) gates: 5 x 64 fp32 (GA_* order below)
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "gdn_common.cuh"
+#include "gdn_kernels.h"
+#include "gdn_tc.cuh"
+
+namespace gdn {
+namespace chunk {
+
+constexpr int kC = 64;  // chunk length (tokens)
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+constexpr uint32_t kRecT = 16384;      // T hi | T lo tile images
+constexpr uint32_t kRecGates = 1280;   // 5 x 64 fp32
+constexpr uint32_t kRecBytes = kRecT + kRecGates;
+static_assert(kRecBytes % 16 == 0, "record alignment");
+
+// gate arrays (per chunk, 64 tokens each): log2-scaled decay prefix g2_t =
+// log2 e * sum_{i<=t} log g_i, beta_t, G_t = exp(g_t), beta_t G_t and the
+// decay to the chunk end exp(g_C - g_t).  Tokens past the sequence end carry
+// beta = 0 and log g = 0 (the prefix stays flat), so they change nothing.
+enum : int { GA_G2 = 0, GA_BETA = 1, GA_G = 2, GA_BG = 3, GA_R = 4, GA_N = 5 };
+
+__host__ __device__ inline int64_t num_slots(int64_t total_tokens, int num_seqs) {
+  return total_tokens / kC + num_seqs + 1;
+}
+
+__device__ __forceinline__ int64_t load_cu(const PrefillParams& p, int i) {
+  return p.cu_is_int64 ? reinterpret_cast<const int64_t*>(p.cu_seqlens)[i]
+                       : (int64_t) reinterpret_cast<const int32_t*>(p.cu_seqlens)[i];
+}
+
+__device__ __forceinline__ int64_t slot_start(int64_t cu_n, int n) { return (cu_n >> 6) + n; }
+
+__device__ __forceinline__ unsigned char* record(const PrefillParams& p, int64_t slot, int h) {
+  return static_cast<unsigned char*>(p.workspace) + ((size_t)slot * (size_t)p.HV + (size_t)h) * kRecBytes;
+}
+
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// (a, b) -> bf16x2 hi and bf16x2 lo with a = hi + lo to ~16 mantissa bits.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf16x2(a, b);
+  lo = pack_bf16x2(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+}
+
+// 16-byte store of 8 bf16 (columns 8*c8 .. 8*c8+7 of `row`) into a SW128 tile.
+__device__ __forceinline__ void st_tile(unsigned char* tile, int row, int c8, uint4 w) {
+  *reinterpret_cast<uint4*>(tile + tc::sw128_offset(row, c8 * 8)) = w;
+}
+
+// Gates of one token (kernel_prefill.py:108-113): log g = -exp(A_log) softplus(a + dt_bias)
+// with softplus(x) = x for x > 20, and beta = sigmoid(b); hardware exp2 / log2.
+__device__ __forceinline__ void token_gates(float eA, float dt_bias, float a, float b, float& lg, float& beta) {
+  const float x = a + dt_bias;
+  const float sp = x > 20.f ? x : kLn2 * tc::lg2_approx(1.f + tc::ex2_approx(x * kLog2e));
+  lg = -eA * sp;
+  beta = 1.f / (1.f + tc::ex2_approx(-b * kLog2e));
+}
+
+}  // namespace chunk
+
+// Launches the prep kernel over every chunk slot and v-head (mapK: the chain
+// kernel's K tensor map, 64-token x 64-feature SW128 boxes).
+cudaError_t launch_prefill_prep(const PrefillParams& p, const CUtensorMap& mapK, cudaStream_t stream);
+
+}  // namespace gdn

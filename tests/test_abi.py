@@ -91,9 +91,17 @@ def test_prefill_rejects_bad_arguments(lib):
     assert call(N=0) == 0
 
 
-def test_workspace_size_is_deterministic(lib):
+def test_workspace_size(lib):
+    """One 17,664-byte record (T hi/lo tiles + 5 gate arrays) per chunk slot and
+    v-head; slots = total_tokens // 64 + num_seqs + 1.  The token-serial paths
+    (forced, or in-kernel q/k normalisation) need no workspace."""
     a = lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
     assert a == lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
+    assert a == (34000 // 64 + 16 + 1) * 32 * 17664
+    assert lib.gdn_prefill_workspace_size(8, 8 * 32768, 16, 32, 128, 0) == (4096 + 9) * 32 * 17664
+    assert lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0x1) == 0  # GDN_FLAG_QK_L2NORM
+    assert lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0x2) == 0  # GDN_FLAG_PREFILL_SERIAL
+    assert lib.gdn_prefill_workspace_size(0, 0, 16, 32, 128, 0) == 0
 
 
 def test_missing_library_fails_loudly(gdn, monkeypatch, tmp_path):
