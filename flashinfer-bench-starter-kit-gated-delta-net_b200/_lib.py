@@ -22,6 +22,7 @@ GDN_FLAG_QK_L2NORM = 0x1
 GDN_FLAG_PREFILL_SERIAL = 0x2
 GDN_DEVERR_WAIT_TIMEOUT = 0x1
 GDN_DEVERR_BAD_SEQLENS = 0x2
+GDN_PREFILL_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 # Every symbol the header declares, with its ctypes signature.
 _P, _I64, _I32, _U32, _F, _SZ = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32,
@@ -45,6 +46,14 @@ SIGNATURES = {
                      _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
                      _P, _SZ, _U32, _P], ctypes.c_int),
     "gdn_prefill_workspace_size": ([_I32, _I64, _I32, _I32, _I32, _U32], ctypes.c_size_t),
+    "gdn_prefill_noalloc": ([_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,  # q, k, v
+                             _P, _I64, _I64,                                   # state
+                             _P, _P, _I64, _P, _P, _I64,                       # A_log, a, dt_bias, b
+                             _P, _I32,                                         # cu_seqlens
+                             _F,                                               # scale
+                             _P, _I64, _I64, _P, _I64, _I64,                   # out, new_state
+                             _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
+                             _U32, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/gdn_b200.h"
@@ -18,6 +19,15 @@ __device__ unsigned int g_gdn_device_error = 0;
 }
 
 namespace {
+
+// Scratch of gdn_prefill_noalloc: a static device array in the library's module, so that
+// entry point allocates nothing.  64 MiB holds 3,799 prepared chunk records (17,664 B each),
+// e.g. total_tokens / 64 + num_seqs + 1 <= 118 chunk slots at 32 v-heads.  No part of it needs
+// to start at zero: the prep kernel writes every record before the chain kernel reads it.
+constexpr size_t kStaticScratchBytes = size_t(GDN_PREFILL_NOALLOC_SCRATCH_BYTES);
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+std::mutex g_scratch_mutex;
+void* g_scratch_addr[64] = {};  // per device, looked up once with that device current
 
 thread_local std::string g_last_error;
 
@@ -247,6 +257,43 @@ int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const voi
                                 : gdn::launch_prefill_serial(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, chunked ? "gdn_prefill (chunked) launch" : "gdn_prefill launch");
   return ok();
+}
+
+int gdn_prefill_noalloc(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
+                        int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h,
+                        const float* state, int64_t state_stride_n, int64_t state_stride_h, const float* A_log,
+                        const void* a, int64_t a_stride_t, const float* dt_bias, const void* b, int64_t b_stride_t,
+                        const void* cu_seqlens, int32_t cu_seqlens_is_int64, float scale, void* out,
+                        int64_t out_stride_t, int64_t out_stride_h, float* new_state, int64_t new_state_stride_n,
+                        int64_t new_state_stride_h, int32_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
+                        int32_t num_v_heads, int32_t head_dim, uint32_t flags, void* stream) {
+  const size_t need =
+      gdn_prefill_workspace_size(num_seqs, total_tokens, num_qk_heads, num_v_heads, head_dim, flags);
+  if (need > kStaticScratchBytes)
+    return fail(GDN_ERR_WORKSPACE,
+                "gdn_prefill_noalloc: the problem needs %zu bytes of scratch, the static scratch holds %zu "
+                "(call gdn_prefill with a workspace instead)",
+                need, kStaticScratchBytes);
+  void* scratch = nullptr;
+  if (need > 0) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(GDN_ERR_UNSUPPORTED, "gdn_prefill_noalloc: device index %d >= 64", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+      void* addr = nullptr;
+      e = cudaGetSymbolAddress(&addr, g_static_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill_noalloc: cudaGetSymbolAddress");
+      g_scratch_addr[dev] = addr;
+    }
+    scratch = g_scratch_addr[dev];
+  }
+  return gdn_prefill(q, q_stride_t, q_stride_h, k, k_stride_t, k_stride_h, v, v_stride_t, v_stride_h, state,
+                     state_stride_n, state_stride_h, A_log, a, a_stride_t, dt_bias, b, b_stride_t, cu_seqlens,
+                     cu_seqlens_is_int64, scale, out, out_stride_t, out_stride_h, new_state, new_state_stride_n,
+                     new_state_stride_h, num_seqs, total_tokens, num_qk_heads, num_v_heads, head_dim, scratch,
+                     scratch ? kStaticScratchBytes : 0, flags, stream);
 }
 
 }  // extern "C"

@@ -63,13 +63,15 @@ def _workspace(device, nbytes: int):
 
 
 def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
-            use_qk_l2norm: bool = False, serial: bool = False, workspace=None):
+            use_qk_l2norm: bool = False, serial: bool = False, workspace=None, no_alloc: bool = False):
     """Destination-passing prefill: writes ``output`` [T,HV,128] bf16 and
     ``new_state`` [N,HV,128,128] fp32 (which may be ``state`` itself).
 
     The chunked tensor-core kernel runs whenever q/k/v rows and strides are
     16-byte aligned and ``use_qk_l2norm`` is off; otherwise (or with
-    ``serial=True``, a cross-checking switch) the token-serial CUDA kernel runs."""
+    ``serial=True``, a cross-checking switch) the token-serial CUDA kernel runs.
+    ``no_alloc=True`` calls ``gdn_prefill_noalloc`` (the library's static scratch
+    instead of a workspace buffer; problems larger than it are rejected)."""
     T, HQ, D = q.shape
     HV = v.shape[1]
     N = cu_seqlens.shape[0] - 1
@@ -87,6 +89,18 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
         state = state.contiguous()
     flags = (_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0) | (_lib.GDN_FLAG_PREFILL_SERIAL if serial else 0)
     lib = _lib.library()
+    if no_alloc:
+        rc = lib.gdn_prefill_noalloc(ptr(q), *seq_head_strides(q, 0, 1), ptr(k), *seq_head_strides(k, 0, 1),
+                                     ptr(v), *seq_head_strides(v, 0, 1),
+                                     ptr(state), *(seq_head_strides(state, 0, 1) if state is not None else (0, 0)),
+                                     ptr(A_log), ptr(a), a.stride(0), ptr(dt_bias), ptr(b), b.stride(0),
+                                     ptr(cu), int(cu.dtype == torch.int64),
+                                     float(scale),
+                                     ptr(output), *seq_head_strides(output, 0, 1),
+                                     ptr(new_state), *seq_head_strides(new_state, 0, 1),
+                                     N, T, HQ, HV, D, flags, stream_handle(q.device))
+        _lib.check(rc)
+        return output, new_state
     need = int(lib.gdn_prefill_workspace_size(N, T, HQ, HV, D, flags))
     if workspace is None:
         workspace = _workspace(q.device, need)

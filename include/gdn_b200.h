@@ -132,6 +132,35 @@ GDN_API int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
 GDN_API size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
                                   int32_t num_v_heads, int32_t head_dim, uint32_t flags);
 
+/*
+ * gdn_prefill without a caller workspace (no counterpart in the reference, whose
+ * prefill needs no scratch): the prepared chunk records live in a static device
+ * array of GDN_PREFILL_NOALLOC_SCRATCH_BYTES inside the library, so the call
+ * allocates nothing.  Arguments and semantics are those of gdn_prefill minus
+ * the workspace.  A problem whose gdn_prefill_workspace_size(...) exceeds the
+ * scratch is rejected with GDN_ERR_WORKSPACE before anything is enqueued.
+ * The scratch is one per device and shared by all calls: calls on that device
+ * that overlap in time (other streams or host threads) race on it.  The first
+ * call on a device looks its address up (cudaGetSymbolAddress) and should come
+ * before any stream capture.  No part of the scratch needs to start at zero.
+ */
+#define GDN_PREFILL_NOALLOC_SCRATCH_BYTES (64u << 20)
+GDN_API int gdn_prefill_noalloc(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                const void* k, int64_t k_stride_t, int64_t k_stride_h,
+                const void* v, int64_t v_stride_t, int64_t v_stride_h,
+                const float* state, int64_t state_stride_n, int64_t state_stride_h,
+                const float* A_log,
+                const void* a, int64_t a_stride_t,
+                const float* dt_bias,
+                const void* b, int64_t b_stride_t,
+                const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                float scale,
+                void* out, int64_t out_stride_t, int64_t out_stride_h,
+                float* new_state, int64_t new_state_stride_n, int64_t new_state_stride_h,
+                int32_t num_seqs, int64_t total_tokens,
+                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                uint32_t flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
