@@ -1,7 +1,7 @@
 // Shared device helpers for the GDN kernels (sm_100a).
 //
 // - bf16 <-> fp32 vector loads/stores
-// - mbarrier + 1-D bulk async copy (cp.async.bulk, TMA engine, no multicast)
+// - mbarrier + 1-D bulk async copy (cp.async.bulk through the TMA engine, one CTA)
 // - bounded waits: every spin has a time limit, after which the kernel records
 //   an error bit in g_gdn_device_error and skips the dependent work instead of
 //   hanging the GPU.

@@ -24,17 +24,16 @@
 // precomputed from the prep kernel (gdn_prefill_prep.cu) as one workspace record
 // per (chunk slot, v-head), bulk-copied into shared memory one chunk ahead.
 //
-// CTA = one (sequence, v-head) chain, 14 warps:
-//   warps 0-7   chain: thread (warp & 3, lane) owns state row v, warp >> 2
-//               selects a column half; S0 hi/lo and G_C scaling, R, deltas,
-//               initial/final state I/O
-//   warps 8-11  P warpgroup: P from Q K^T (warps 10, 11, whose TMEM lanes hold
-//               the Q rows) and Q scaled by G in place (warps 8, 9) one chunk
-//               ahead; the outputs of the previous chunk (TMEM -> bf16 rows in
-//               shared memory -> bulk stores, one per token row)
-//   warp 12     TMA producer: T and gate records (bulk), K, Q (128B-swizzled
-//               tiles), V (plain); all double-buffered except V
-//   warp 13     TMEM allocator and MMA issuer
+// CTA = one (sequence, v-head) chain, 4 kCW + 6 warps:
+//   4 kCW chain warps: thread (warp & 3, lane) owns state row v, warp >> 2
+//               selects 1/kCW of the columns; S0 hi/lo and G_C scaling, R,
+//               deltas, initial/final state I/O
+//   4 P warps   P from Q K^T one chunk ahead (Q rows on all 128 TMEM lanes),
+//               G-scaling of S0 Q^T in TMEM, the outputs of the previous chunk
+//               (TMEM -> bf16 rows in shared memory -> one TMA store)
+//   1 TMA warp  T and gate records (bulk), K, Q (128B-swizzled tiles), V
+//               (plain); all double-buffered except V
+//   1 MMA warp  TMEM allocator and MMA issuer
 // Per chunk the state chain is S0 hi/lo -> [S0 [K;Q]^T] -> R -> [R^T T^T] ->
 // deltas -> [S += Dt^T K] -> next chunk; Q K^T, the output MMA (D^T P^T), the
 // output stores and the P work overlap it.  Hand-offs are mbarriers; every wait is
@@ -50,16 +49,26 @@ namespace {
 
 using namespace chunk;
 
-constexpr int kThreads = 448;   // 14 warps
-constexpr int kChainThreads = 256;
-constexpr int kWarpTma = 12, kWarpMma = 13;
+// Chain warps per TMEM lane quarter (the warp's quarter is warp % 4, which is also
+// its scheduler): each chain thread owns one state row and 1/kCW of the columns.
+#ifndef GDN_CHAIN_WARPS_PER_QUARTER
+#define GDN_CHAIN_WARPS_PER_QUARTER 4
+#endif
+constexpr int kCW = GDN_CHAIN_WARPS_PER_QUARTER;
+constexpr int kChainWarps = 4 * kCW;
+constexpr int kChainThreads = 32 * kChainWarps;
+constexpr int kWarpP0 = kChainWarps;  // P warpgroup: 4 warps after the chain warps
+constexpr int kWarpTma = kChainWarps + 4, kWarpMma = kChainWarps + 5;
+constexpr int kThreads = 32 * (kChainWarps + 6);
+constexpr int kStateCols = 128 / kCW, kTokCols = 64 / kCW;  // per chain thread
+static_assert(kCW == 2 || kCW == 4, "chain split");
 constexpr uint32_t kTmemCols = 512;
 
 // TMEM column map (lanes = state row v unless noted)
 constexpr uint32_t kTmS = 0;      // [0,128)  state S[v][k], fp32
-constexpr uint32_t kTmD1 = 128;   // 2 buffers [128,256), [256,384), fp32: cols 0-63 [K; Q] K^T (Q rows on
-                                  //   lanes 64-127), then S0 K^T, then D^T; cols 64-127 S0 Q^T, scaled by G
-                                  //   in place, + D^T P^T = O^T (unscaled)
+constexpr uint32_t kTmD1 = 128;   // 2 buffers [128,256), [256,384), fp32: cols 0-63 S0 Q^T, scaled by G in
+                                  //   place, + D^T P^T = O^T (unscaled); cols 64-127 [Q; Q] K^T scratch
+                                  //   (lanes = token, twice), then S0 K^T, then D^T
                                   // [384,512) bf16 A operands, two per column, reused along the chain:
 constexpr uint32_t kTmS0hi = 384; //   S0 hi [384,448), S0 lo [448,512)           (S0 split .. MMA1)
 constexpr uint32_t kTmS0lo = 448;
@@ -69,21 +78,24 @@ constexpr uint32_t kTmDthi = 448; //   Dt hi [448,480), Dt lo [480,512)         
 constexpr uint32_t kTmDtlo = 480;
 
 // Shared-memory map (offsets from a 1024-byte aligned base)
-constexpr uint32_t kSmKQ = 0;          // 2 stages x 32 KB: [tile d0-63 | tile d64-127], rows 0-63 K, 64-127 Q
-constexpr uint32_t kKQStage = 32768;
-constexpr uint32_t kKQTile = 16384;    // one 64-column SW128 tile of 128 rows
-constexpr uint32_t kSmV = 65536;       // V, plain row-major [64][128] bf16 (16 KB)
-constexpr uint32_t kSmD = 81920;       // D^T bf16 SW128 tile [128 x 64] (A of the output MMA)
-constexpr uint32_t kSmT = 98304;       // 2 stages x (T hi | T lo: 2 tiles [64 x 64]) (record bytes 0-16383)
+constexpr uint32_t kSmKQ = 0;          // 2 stages x 48 KB: [tile d0-63 | tile d64-127]; in each 64-column
+constexpr uint32_t kKQStage = 49152;   // SW128 tile rows 0-63 Q, 64-127 Q again, 128-191 K, so that
+constexpr uint32_t kKQTile = 24576;    // [Q; Q] (A of Q K^T: the Q rows on all 128 TMEM lanes) and
+constexpr uint32_t kRowsQ2 = 8192;     // [Q; K] (B of the first MMA) are both 128 contiguous rows
+constexpr uint32_t kRowsK = 16384;
+constexpr uint32_t kSmV = 98304;       // V, plain row-major [64][128] bf16 (16 KB)
+constexpr uint32_t kSmD = 114688;      // D^T bf16 SW128 tile [128 x 64] (A of the output MMA)
+constexpr uint32_t kSmT = 131072;      // 2 stages x (T hi | T lo: 2 tiles [64 x 64]) (record bytes 0-16383)
 constexpr uint32_t kTStage = kRecT;
-constexpr uint32_t kSmP = 131072;      // P tile [64 x 64]
-constexpr uint32_t kSmO = 139264;      // output rows of one chunk, [64 tokens][128] bf16 (bulk-store source)
-constexpr uint32_t kSmGate = 155648;   // 2 stages x gate arrays (record bytes 16384-17663)
-constexpr uint32_t kSmBar = 158208;    // mbarriers (32 x 8 B)
-constexpr uint32_t kSmMisc = 158464;   // tmem base slot, abort flag
-constexpr uint32_t kSmBytes = 158528;
+constexpr uint32_t kSmP = 163840;      // P tile [64 x 64]
+constexpr uint32_t kSmO = 172032;      // output rows of one chunk, [64 tokens][128] bf16 (TMA-store source)
+constexpr uint32_t kSmGate = 188416;   // 2 stages x gate arrays (record bytes 16384-17663)
+constexpr uint32_t kSmBar = 190976;    // mbarriers (32 x 8 B)
+constexpr uint32_t kSmMisc = 191232;   // tmem base slot, abort flag
+constexpr uint32_t kSmBytes = 191296;
 constexpr uint32_t kSmAlloc = kSmBytes + 1024;  // + alignment slack
-static_assert(kSmT + 2 * kTStage <= kSmP && kSmO + 16384 <= kSmGate && kSmGate + 2 * kRecGates <= kSmBar,
+static_assert(kSmKQ + 2 * kKQStage <= kSmV && kSmT + 2 * kTStage <= kSmP && kSmO + 16384 <= kSmGate &&
+                  kSmGate + 2 * kRecGates <= kSmBar,
               "smem map");
 static_assert(kSmAlloc <= 232448, "smem budget");
 
@@ -121,15 +133,15 @@ struct Smem {
   __device__ uint32_t addr(uint32_t off) const { return smem_u32(base + off); }
 };
 
-// Bounded wait that also gives up as soon as another role has aborted.  Polls
-// without suspending for the first few microseconds (hand-offs along the chain
-// are a few hundred cycles apart, and a suspended thread wakes up late), then
-// lets the thread be suspended between tests.
+// Bounded wait that also gives up as soon as another role has aborted: first
+// blocking tests (the hardware suspends the thread until the phase completes or
+// a short time limit passes, so a waiting thread takes no issue slots), then
+// tests with a longer suspend hint between abort and time-limit checks.
 __device__ __forceinline__ bool wait_bar(const Smem& sm, uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
 #pragma unroll 1
-  for (int k = 0; k < 512; ++k)
-    if (mbar_test_wait(addr, parity)) return true;
+  for (int k = 0; k < 64; ++k)
+    if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
 #pragma unroll 1
   while (true) {
@@ -220,12 +232,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_g2s(sm.base + kSmGate + s * kRecGates, rec + kRecT, kRecGates, sm.bar(B_GATES + s));
         if (i >= 2 && !wait_bar(sm, sm.bar(B_KQ_EMPTY + s), ph)) break;
         uint64_t* full = sm.bar(B_KQ_FULL + s);
-        mbar_arrive_expect_tx(full, 4 * 8192);
+        mbar_arrive_expect_tx(full, 6 * 8192);
         unsigned char* kq = sm.base + kSmKQ + s * kKQStage;
-        tc::tma_load_3d(kq, &mapK, 0, qh, z, full);
-        tc::tma_load_3d(kq + kKQTile, &mapK, 64, qh, z, full);
-        tc::tma_load_3d(kq + 8192, &mapQ, 0, qh, z, full);
-        tc::tma_load_3d(kq + kKQTile + 8192, &mapQ, 64, qh, z, full);
+#pragma unroll
+        for (int f = 0; f < 2; ++f) {  // the two 64-feature tiles: Q, Q, K
+          tc::tma_load_3d(kq + f * kKQTile, &mapQ, 64 * f, qh, z, full);
+          tc::tma_load_3d(kq + f * kKQTile + kRowsQ2, &mapQ, 64 * f, qh, z, full);
+          tc::tma_load_3d(kq + f * kKQTile + kRowsK, &mapK, 64 * f, qh, z, full);
+        }
         if (i >= 1 && !wait_bar(sm, sm.bar(B_V_EMPTY), (i - 1) & 1)) break;
         mbar_arrive_expect_tx(sm.bar(B_V_FULL), 16384);
         tc::tma_load_3d(sm.base + kSmV, &mapV, 0, h, z, sm.bar(B_V_FULL));
@@ -258,18 +272,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dP = tc::kmajor_desc(sm.addr(kSmP), 0, 0);
       const uint64_t dKQ0 = tc::kmajor_desc(sm.addr(kSmKQ), 0, 0);
       const uint64_t dKQ1 = tc::kmajor_desc(sm.addr(kSmKQ + kKQStage), 0, 0);
-      const uint64_t dKmn0 = tc::mnmajor_desc(sm.addr(kSmKQ), kKQTile, 0);
-      const uint64_t dKmn1 = tc::mnmajor_desc(sm.addr(kSmKQ + kKQStage), kKQTile, 0);
-      // [K; Q] K^T of chunk j into D1[j & 1] columns 0-63 (its Q rows land on lanes 64-127);
-      // that half of the buffer was last read by the deltas of chunk j - 2
+      const uint64_t dKmn0 = tc::mnmajor_desc(sm.addr(kSmKQ + kRowsK), kKQTile, 0);
+      const uint64_t dKmn1 = tc::mnmajor_desc(sm.addr(kSmKQ + kKQStage + kRowsK), kKQTile, 0);
+      constexpr uint64_t kOffQ2 = kRowsQ2 >> 4, kOffK = kRowsK >> 4;  // descriptor offsets of the [Q; K] and K rows
+      // [Q; Q] K^T of chunk j into D1[j & 1] columns 64-127 (Q K^T on lanes 0-63 and again on
+      // 64-127); that half of the buffer was last read by the deltas of chunk j - 2
       auto issue_kkqk = [&](int j) -> bool {
         if (!wait_bar(sm, sm.bar(B_KQ_FULL + (j & 1)), (j >> 1) & 1)) return false;
         tc::fence_after_sync();
         const uint64_t d = (j & 1) ? dKQ1 : dKQ0;
-        const uint32_t dst = tmem + kTmD1 + (uint32_t)(j & 1) * 128;
+        const uint32_t dst = tmem + kTmD1 + (uint32_t)(j & 1) * 128 + 64;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(dst, d + kmajor_step(kKQTile, ks), d + kmajor_step(kKQTile, ks), id_n64, ks > 0);
+          tc::mma_bf16(dst, d + kmajor_step(kKQTile, ks), d + kOffK + kmajor_step(kKQTile, ks), id_n64, ks > 0);
         tc::mma_commit(sm.bar(B_KKQK));
         return true;
       };
@@ -279,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t dK = s ? dKQ1 : dKQ0;
         const uint64_t dKmn = s ? dKmn1 : dKmn0;
         const uint32_t d1 = tmem + kTmD1 + (uint32_t)s * 128;
-        // MMA1: D1 = S0_hi [K; Q]^T (N = 128), then D1[:, K part] += S0_lo K^T; the buffer's
+        // MMA1: D1 = S0_hi [Q; K]^T (N = 128), then D1[:, K part] += S0_lo K^T; the buffer's
         // Q K^T has been read and its outputs of chunk i - 2 stored
         if (!wait_bar(sm, sm.bar(B_S0_READY), i & 1)) break;
         if (!wait_bar(sm, sm.bar(B_D0_FREE), i & 1)) break;
@@ -287,27 +302,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16_ta(d1, tmem + kTmS0hi + 8 * ks, dK + kmajor_step(kKQTile, ks), id_n128, ks > 0);
+          tc::mma_bf16_ta(d1, tmem + kTmS0hi + 8 * ks, dK + kOffQ2 + kmajor_step(kKQTile, ks), id_n128, ks > 0);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16_ta(d1, tmem + kTmS0lo + 8 * ks, dK + kmajor_step(kKQTile, ks), id_n64, true);
+          tc::mma_bf16_ta(d1 + 64, tmem + kTmS0lo + 8 * ks, dK + kOffK + kmajor_step(kKQTile, ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA1));
         // next chunk's Q K^T while the chain computes R
         if (i + 1 < nchunks && !issue_kkqk(i + 1)) break;
-        // MMA2: D^T = R^T T^T into D1 columns 0-63 (R and T split hi/lo: 3 products)
+        // MMA2: D^T = R^T T^T into D1 columns 64-127 (R and T split hi/lo: 3 products)
         if (!wait_bar(sm, sm.bar(B_T_FULL + s), (i >> 1) & 1)) break;
         if (!wait_bar(sm, sm.bar(B_R_READY), i & 1)) break;
         tc::fence_after_sync();
         const uint64_t dT = s ? dT1 : dT0;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16_ta(d1, tmem + kTmRhi + 8 * ks, dT + kmajor_step(0, ks), id_n64, ks > 0);
+          tc::mma_bf16_ta(d1 + 64, tmem + kTmRhi + 8 * ks, dT + kmajor_step(0, ks), id_n64, ks > 0);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16_ta(d1, tmem + kTmRlo + 8 * ks, dT + kmajor_step(0, ks), id_n64, true);
+          tc::mma_bf16_ta(d1 + 64, tmem + kTmRlo + 8 * ks, dT + kmajor_step(0, ks), id_n64, true);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16_ta(d1, tmem + kTmRhi + 8 * ks, dT + kTlo + kmajor_step(0, ks), id_n64, true);
+          tc::mma_bf16_ta(d1 + 64, tmem + kTmRhi + 8 * ks, dT + kTlo + kmajor_step(0, ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA2));
         tc::mma_commit(sm.bar(B_T_EMPTY + s));
         // state first: S += Dt^T K (hi/lo); then the output: D1[:, O part] += D^T P^T
@@ -325,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16(d1 + 64, dD + kmajor_step(0, ks), dP + kmajor_step(0, ks), id_n64, true);
+          tc::mma_bf16(d1, dD + kmajor_step(0, ks), dP + kmajor_step(0, ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA3));
       }
       // drain: every MMA issued above has completed before TMEM is released
@@ -334,34 +349,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   // ======================================================================= P warpgroup
-  else if (warp >= 8) {
-    const int pth = tid - 256;  // 0..127; TMEM lane quarter = warp & 3
-    const int row = pth & 63;
+  else if (warp >= kWarpP0) {
+    const int pth = tid - 32 * kWarpP0;  // 0..127; TMEM lane quarter = warp & 3
     const bool pleader = pth == 0;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32);
     const int v = (warp & 3) * 32 + lane;  // state row (TMEM lane) in the O^T passes
     __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(sm.base + kSmO);
     const float scale = p.scale;
-    // outputs of chunk ci: o[t][v] = scale * O^T[v][t] (D1 buffer ci & 1, columns 64-127),
+    // outputs of chunk ci: o[t][v] = scale * O^T[v][t] (D1 buffer ci & 1, columns 0-63),
     // staged as bf16 rows in shared memory, then stored by TMA
     auto emit_out = [&](int ci) {
       const int64_t rem = len - (int64_t)ci * kC;
       const int nvalid = rem < kC ? (int)rem : kC;
-      if (warp == 8) tc::bulk_wait_read_all();  // the previous chunk's row stores have read the stage
+      if (warp == kWarpP0) tc::bulk_wait_read_all();  // the previous chunk's row stores have read the stage
       named_sync(2, 128);
 #pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float x[32];
-        tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, kTmD1 + (uint32_t)(ci & 1) * 128 + 64 + half * 32), x);
+      for (int q16 = 0; q16 < 4; ++q16) {
+        float x[16];
+        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, kTmD1 + (uint32_t)(ci & 1) * 128 + q16 * 16), x);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int u = 0; u < 32; ++u) ostage[(half * 32 + u) * kHeadDim + v] = __float2bfloat16_rn(scale * x[u]);
+        for (int u = 0; u < 16; ++u) ostage[(q16 * 16 + u) * kHeadDim + v] = __float2bfloat16_rn(scale * x[u]);
       }
       tc::fence_before_sync();
       tc::fence_proxy_async_smem();
       named_sync(2, 128);
       if (pleader) mbar_arrive(sm.bar(B_OUT_DONE + (ci & 1)));
-      if (warp == 8) {
+      if (warp == kWarpP0) {
         if (nvalid == kC) {  // whole chunk: one tiled store of the [64 x 128] box
           if (lane == 0) tc::tma_store_3d(&mapO, 0, h, (int)(t0 + (int64_t)ci * kC), ostage);
         } else {  // a sequence's last, partial chunk: only its own rows
@@ -380,23 +394,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_wait(sm, B_GATES + s, (i >> 1) & 1, 2, 128, pleader)) break;
       if (!group_wait(sm, B_KKQK, i & 1, 2, 128, pleader)) break;
       tc::fence_after_sync();
-      uint32_t prow[32];
-      if (pth >= 64) {
-        const float* g2 = sm.gate(s, GA_G2);
-        const float gt = g2[row];
-        const uint32_t d0 = tc::tmem_addr(tmem, lane_base, d1);
+      // P rows from Q K^T (D1 columns 64-127; every lane quarter holds the 64 Q rows):
+      // thread (row r, column half ch) keeps P[r][32 ch .. 32 ch + 31] in registers until
+      // the P tile is free; P[t][j] = exp(g_t - g_j) q_t.k_j for j <= t
+      const int ch = (warp & 3) >> 1, prow_r = ((warp & 1) << 5) | lane;
+      uint32_t prow[16];
+      {
+        const float* g2 = sm.gate(s, GA_G2) + 32 * ch;
+        const float gt = sm.gate(s, GA_G2)[prow_r];
+        const uint32_t d0 = tc::tmem_addr(tmem, lane_base, d1 + 64 + 32 * ch);
 #pragma unroll
-        for (int j8 = 0; j8 < 8; ++j8) {
-          float w8[8];
-          tc::tmem_ld8(d0 + j8 * 8, w8);
-          const float4 g0 = *reinterpret_cast<const float4*>(g2 + j8 * 8);
-          const float4 g1 = *reinterpret_cast<const float4*>(g2 + j8 * 8 + 4);
+        for (int q16 = 0; q16 < 2; ++q16) {
+          float w[16];
+          tc::tmem_ld16(d0 + q16 * 16, w);
           tc::tmem_wait_ld();
-          const float gj[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          if (32 * ch + 16 * q16 <= prow_r) {  // some j <= r in this group of 16
 #pragma unroll
-          for (int u = 0; u < 8; ++u) w8[u] = j8 * 8 + u <= row ? tc::ex2_approx(gt - gj[u]) * w8[u] : 0.f;
+            for (int u4 = 0; u4 < 4; ++u4) {
+              const float4 gj = *reinterpret_cast<const float4*>(g2 + 16 * q16 + 4 * u4);
+              const int j = 32 * ch + 16 * q16 + 4 * u4;
+              w[4 * u4 + 0] = j + 0 <= prow_r ? tc::ex2_approx(gt - gj.x) * w[4 * u4 + 0] : 0.f;
+              w[4 * u4 + 1] = j + 1 <= prow_r ? tc::ex2_approx(gt - gj.y) * w[4 * u4 + 1] : 0.f;
+              w[4 * u4 + 2] = j + 2 <= prow_r ? tc::ex2_approx(gt - gj.z) * w[4 * u4 + 2] : 0.f;
+              w[4 * u4 + 3] = j + 3 <= prow_r ? tc::ex2_approx(gt - gj.w) * w[4 * u4 + 3] : 0.f;
+            }
+          } else {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) prow[j8 * 4 + u] = pack_bf16x2(w8[2 * u], w8[2 * u + 1]);
+            for (int u = 0; u < 16; ++u) w[u] = 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) prow[8 * q16 + u] = pack_bf16x2(w[2 * u], w[2 * u + 1]);
         }
       }
       tc::fence_before_sync();
@@ -404,11 +431,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (pleader) mbar_arrive(sm.bar(B_D0_FREE));
       // ---- P tile, once the output MMA of chunk i-1 has read the previous one ----
       if (i >= 1 && !group_wait(sm, B_MMA3, (i - 1) & 1, 2, 128, pleader)) break;
-      if (pth >= 64) {
+      {
         unsigned char* pt = sm.base + kSmP;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8)
-          st_tile(pt, row, c8, make_uint4(prow[c8 * 4], prow[c8 * 4 + 1], prow[c8 * 4 + 2], prow[c8 * 4 + 3]));
+        for (int c8 = 0; c8 < 4; ++c8)
+          st_tile(pt, prow_r, 4 * ch + c8,
+                  make_uint4(prow[c8 * 4], prow[c8 * 4 + 1], prow[c8 * 4 + 2], prow[c8 * 4 + 3]));
       }
       tc::fence_proxy_async_smem();
       // ---- outputs of chunk i-1 (its output MMA completed above) ----
@@ -423,20 +451,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const float* G = sm.gate(s, GA_G);
 #pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          float x[32];
-          const uint32_t ta = tc::tmem_addr(tmem, lane_base, d1 + 64 + half * 32);
-          tc::tmem_ld32(ta, x);
+        for (int q16 = 0; q16 < 4; ++q16) {
+          float x[16];
+          const uint32_t ta = tc::tmem_addr(tmem, lane_base, d1 + q16 * 16);
+          tc::tmem_ld16(ta, x);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int u4 = 0; u4 < 8; ++u4) {
-            const float4 g4 = *reinterpret_cast<const float4*>(G + half * 32 + 4 * u4);
+          for (int u4 = 0; u4 < 4; ++u4) {
+            const float4 g4 = *reinterpret_cast<const float4*>(G + q16 * 16 + 4 * u4);
             x[4 * u4 + 0] *= g4.x;
             x[4 * u4 + 1] *= g4.y;
             x[4 * u4 + 2] *= g4.z;
             x[4 * u4 + 3] *= g4.w;
           }
-          tc::tmem_st32(ta, x);
+          tc::tmem_st16(ta, x);
         }
         tc::tmem_wait_st();
       }
@@ -452,20 +480,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
       emit_out(nchunks - 1);
     }
-    if (warp == 8) tc::bulk_wait_all();
+    if (warp == kWarpP0) tc::bulk_wait_all();
   }
   // ======================================================================= chain warps
   else {
-    const int quarter = warp & 3, hsel = warp >> 2;
-    const int v = quarter * 32 + lane;  // state row / TMEM lane
+    const int quarter = warp & 3, hsel = warp >> 2;  // hsel: column slice 0..kCW-1
+    const int v = quarter * 32 + lane;               // state row / TMEM lane
     const uint32_t lane_base = (uint32_t)(quarter * 32);
     const bool leader = tid == 0;
-    // initial state (this thread's 64-column half) -> TMEM S
+    const int sc = hsel * kStateCols;  // this thread's state columns [sc, sc + kStateCols)
+    const int tb = hsel * kTokCols;    // this thread's token columns [tb, tb + kTokCols)
+    // initial state (this thread's columns) -> TMEM S
     {
       const float* src =
-          p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh + (size_t)v * kHeadDim + hsel * 64 : nullptr;
+          p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh + (size_t)v * kHeadDim + sc : nullptr;
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 16) {
+      for (int c0 = 0; c0 < kStateCols; c0 += 16) {
         float x[16];
 #pragma unroll
         for (int q = 0; q < 16; q += 4) {
@@ -475,13 +505,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           x[q + 2] = f.z;
           x[q + 3] = f.w;
         }
-        tc::tmem_st16(tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64 + c0), x);
+        tc::tmem_st16(tc::tmem_addr(tmem, lane_base, kTmS + sc + c0), x);
       }
       tc::tmem_wait_st();
     }
     unsigned char* dtile = sm.base + kSmD;
     const __nv_bfloat16* vt = reinterpret_cast<const __nv_bfloat16*>(sm.base + kSmV);
-    const int tb = hsel * 32;  // this thread's token columns [tb, tb + 32)
     for (int i = 0; i < nchunks; ++i) {
       const int s = i & 1;
       const uint32_t d1 = kTmD1 + (uint32_t)s * 128;
@@ -490,54 +519,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- S0 hi/lo into TMEM (A of the first MMA) ----
       if (i > 0 && !group_wait(sm, B_MMA4 + ((i - 1) & 1), ((i - 1) >> 1) & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
-      {
-        float x[2][32];
-        const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64);
-        tc::tmem_ld32(ta, x[0]);
-        tc::tmem_ld32(ta + 32, x[1]);
+#pragma unroll
+      for (int piece = 0; piece < kStateCols / 16; ++piece) {
+        float x[16];
+        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, kTmS + sc + piece * 16), x);
         tc::tmem_wait_ld();
+        uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u) split2(x[half][2 * u], x[half][2 * u + 1], hi[u], lo[u]);
-          tc::tmem_st16u(tc::tmem_addr(tmem, lane_base, kTmS0hi + hsel * 32 + half * 16), hi);
-          tc::tmem_st16u(tc::tmem_addr(tmem, lane_base, kTmS0lo + hsel * 32 + half * 16), lo);
-        }
-        tc::tmem_wait_st();
+        for (int u = 0; u < 8; ++u) split2(x[2 * u], x[2 * u + 1], hi[u], lo[u]);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmS0hi + sc / 2 + piece * 8), hi);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmS0lo + sc / 2 + piece * 8), lo);
       }
+      tc::tmem_wait_st();
       tc::fence_before_sync();
       named_sync(1, kChainThreads);
       if (leader) mbar_arrive(sm.bar(B_S0_READY));
       // ---- S <- G_C * S while the first MMA runs (it reads only the hi/lo copies; the
       //      state MMA of this chunk comes after the deltas) ----
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        float x[32];
-        const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64 + half * 32);
-        tc::tmem_ld32(ta, x);
+#pragma unroll
+      for (int piece = 0; piece < kStateCols / 16; ++piece) {
+        float x[16];
+        const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + sc + piece * 16);
+        tc::tmem_ld16(ta, x);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 32; ++q) x[q] *= GC;
-        tc::tmem_st32(ta, x);
+        for (int q = 0; q < 16; ++q) x[q] *= GC;
+        tc::tmem_st16(ta, x);
       }
       tc::tmem_wait_st();
-      // ---- R^T = beta V^T - beta G (S0 K^T), split hi/lo into TMEM (32 token columns per thread) ----
+      // ---- R^T = beta V^T - beta G (S0 K^T), split hi/lo into TMEM (16 token columns per thread) ----
       if (!group_wait(sm, B_V_FULL, i & 1, 1, kChainThreads, leader)) break;
       if (!group_wait(sm, B_MMA1, i & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
-      {
-        float x[32];
-        tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, d1 + tb), x);
-        float vv[32];
 #pragma unroll
-        for (int u = 0; u < 32; ++u) vv[u] = __bfloat162float(vt[(tb + u) * kHeadDim + v]);
-        const float* bet = sm.gate(s, GA_BETA) + tb;
-        const float* bg = sm.gate(s, GA_BG) + tb;
+      for (int piece = 0; piece < kTokCols / 16; ++piece) {
+        const int t0c = tb + piece * 16;
+        float x[16];
+        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, d1 + 64 + t0c), x);
+        float vv[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) vv[u] = __bfloat162float(vt[(t0c + u) * kHeadDim + v]);
+        const float* bet = sm.gate(s, GA_BETA) + t0c;
+        const float* bg = sm.gate(s, GA_BG) + t0c;
         tc::tmem_wait_ld();
-        uint32_t hi[16], lo[16];
+        uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int u4 = 0; u4 < 8; ++u4) {
+        for (int u4 = 0; u4 < 4; ++u4) {
           const float4 b4 = *reinterpret_cast<const float4*>(bet + 4 * u4);
           const float4 g4 = *reinterpret_cast<const float4*>(bg + 4 * u4);
           const float r0 = fmaf(b4.x, vv[4 * u4 + 0], -g4.x * x[4 * u4 + 0]);
@@ -547,10 +574,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           split2(r0, r1, hi[2 * u4], lo[2 * u4]);
           split2(r2, r3, hi[2 * u4 + 1], lo[2 * u4 + 1]);
         }
-        tc::tmem_st16u(tc::tmem_addr(tmem, lane_base, kTmRhi + hsel * 16), hi);
-        tc::tmem_st16u(tc::tmem_addr(tmem, lane_base, kTmRlo + hsel * 16), lo);
-        tc::tmem_wait_st();
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRhi + t0c / 2), hi);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRlo + t0c / 2), lo);
       }
+      tc::tmem_wait_st();
       tc::fence_before_sync();
       named_sync(1, kChainThreads);
       if (leader) {
@@ -560,20 +587,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- deltas: D^T (bf16 tile, output MMA) and Dt^T = D^T exp(gC - g) (hi/lo into TMEM, state MMA) ----
       if (!group_wait(sm, B_MMA2, i & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
-      {
-        float d[32];
-        tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, d1 + tb), d);
-        const float* rr = sm.gate(s, GA_R) + tb;
-        tc::tmem_wait_ld();
-        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
+      for (int piece = 0; piece < kTokCols / 16; ++piece) {
+        const int t0c = tb + piece * 16;
+        float d[16];
+        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, d1 + 64 + t0c), d);
+        const float* rr = sm.gate(s, GA_R) + t0c;
+        tc::tmem_wait_ld();
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int c8 = 0; c8 < 2; ++c8) {
           uint4 dd;
           dd.x = pack_bf16x2(d[8 * c8 + 0], d[8 * c8 + 1]);
           dd.y = pack_bf16x2(d[8 * c8 + 2], d[8 * c8 + 3]);
           dd.z = pack_bf16x2(d[8 * c8 + 4], d[8 * c8 + 5]);
           dd.w = pack_bf16x2(d[8 * c8 + 6], d[8 * c8 + 7]);
-          st_tile(dtile, v, (tb >> 3) + c8, dd);
+          st_tile(dtile, v, (t0c >> 3) + c8, dd);
           const float4 r0 = *reinterpret_cast<const float4*>(rr + 8 * c8);
           const float4 r1 = *reinterpret_cast<const float4*>(rr + 8 * c8 + 4);
           split2(d[8 * c8 + 0] * r0.x, d[8 * c8 + 1] * r0.y, hi[4 * c8 + 0], lo[4 * c8 + 0]);
@@ -581,10 +610,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           split2(d[8 * c8 + 4] * r1.x, d[8 * c8 + 5] * r1.y, hi[4 * c8 + 2], lo[4 * c8 + 2]);
           split2(d[8 * c8 + 6] * r1.z, d[8 * c8 + 7] * r1.w, hi[4 * c8 + 3], lo[4 * c8 + 3]);
         }
-        tc::tmem_st16u(tc::tmem_addr(tmem, lane_base, kTmDthi + hsel * 16), hi);
-        tc::tmem_st16u(tc::tmem_addr(tmem, lane_base, kTmDtlo + hsel * 16), lo);
-        tc::tmem_wait_st();
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDthi + t0c / 2), hi);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDtlo + t0c / 2), lo);
       }
+      tc::tmem_wait_st();
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       named_sync(1, kChainThreads);
@@ -600,11 +629,11 @@ __global__ void __launch_bounds__(kThreads, 1)
            !*sm.abort_flag();
     if (ok) {
       tc::fence_after_sync();
-      float* dst = p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh + (size_t)v * kHeadDim + hsel * 64;
+      float* dst = p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh + (size_t)v * kHeadDim + sc;
 #pragma unroll 1
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int c8 = 0; c8 < kStateCols / 8; ++c8) {
         float x[8];
-        tc::tmem_ld8(tc::tmem_addr(tmem, lane_base, kTmS + hsel * 64 + c8 * 8), x);
+        tc::tmem_ld8(tc::tmem_addr(tmem, lane_base, kTmS + sc + c8 * 8), x);
         tc::tmem_wait_ld();
         *reinterpret_cast<float4*>(dst + c8 * 8) = make_float4(x[0], x[1], x[2], x[3]);
         *reinterpret_cast<float4*>(dst + c8 * 8 + 4) = make_float4(x[4], x[5], x[6], x[7]);

@@ -121,20 +121,39 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-// d += M[m0.., k0..] (16 x 8, row-major in AT at row offset mr, col offset mc) x
-//      N[k0.., n0..] (8 x 8, row-major in AT at nr, nc)
-__device__ __forceinline__ void mma_step(float (&d)[4], const float* AT, int mr, int mc, int nr, int nc, int lane) {
+struct FragA {
+  uint32_t h[4], l[4];
+};
+struct FragB {
+  uint32_t h[2], l[2];
+};
+// A fragment of the 16 x 8 block of AT at rows mr.., cols mc..
+__device__ __forceinline__ FragA load_a(const float* AT, int mr, int mc, int lane) {
   const int g = lane >> 2, t = lane & 3;
-  uint32_t ah[4], al[4], bh[2], bl[2];
-  split_tf32(AT[(mr + g) * kLd + mc + t], ah[0], al[0]);
-  split_tf32(AT[(mr + g + 8) * kLd + mc + t], ah[1], al[1]);
-  split_tf32(AT[(mr + g) * kLd + mc + t + 4], ah[2], al[2]);
-  split_tf32(AT[(mr + g + 8) * kLd + mc + t + 4], ah[3], al[3]);
-  split_tf32(AT[(nr + t) * kLd + nc + g], bh[0], bl[0]);
-  split_tf32(AT[(nr + t + 4) * kLd + nc + g], bh[1], bl[1]);
-  mma_tf32(d, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
-  mma_tf32(d, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+  FragA f;
+  split_tf32(AT[(mr + g) * kLd + mc + t], f.h[0], f.l[0]);
+  split_tf32(AT[(mr + g + 8) * kLd + mc + t], f.h[1], f.l[1]);
+  split_tf32(AT[(mr + g) * kLd + mc + t + 4], f.h[2], f.l[2]);
+  split_tf32(AT[(mr + g + 8) * kLd + mc + t + 4], f.h[3], f.l[3]);
+  return f;
+}
+// B fragment of the 8 x 8 block of AT at rows nr.. (K), cols nc.. (N)
+__device__ __forceinline__ FragB load_b(const float* AT, int nr, int nc, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  FragB f;
+  split_tf32(AT[(nr + t) * kLd + nc + g], f.h[0], f.l[0]);
+  split_tf32(AT[(nr + t + 4) * kLd + nc + g], f.h[1], f.l[1]);
+  return f;
+}
+// d += A B with the 3-term split
+__device__ __forceinline__ void mma3(float (&d)[4], const FragA& a, const FragB& b) {
+  mma_tf32(d, a.l[0], a.l[1], a.l[2], a.l[3], b.h[0], b.h[1]);
+  mma_tf32(d, a.h[0], a.h[1], a.h[2], a.h[3], b.l[0], b.l[1]);
+  mma_tf32(d, a.h[0], a.h[1], a.h[2], a.h[3], b.h[0], b.h[1]);
+}
+// d += M[mr.., mc..] (16 x 8) x N[nr.., nc..] (8 x 8), blocks of AT
+__device__ __forceinline__ void mma_step(float (&d)[4], const float* AT, int mr, int mc, int nr, int nc, int lane) {
+  mma3(d, load_a(AT, mr, mc, lane), load_b(AT, nr, nc, lane));
 }
 // store a 16 x 8 accumulator tile (times `sign`) at AT rows r0.., cols c0..
 __device__ __forceinline__ void st_tile_f32(float* AT, int r0, int c0, const float (&d)[4], float sign, int lane) {
@@ -177,8 +196,9 @@ __device__ __forceinline__ void solve_merge32(float* AT, int p, int bar) {
     float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
     for (int ks = w; ks < 4; ++ks) {
-      mma_step(d0, AT, 32, 8 * ks, 8 * ks, n0, lane);
-      mma_step(d1, AT, 48, 8 * ks, 8 * ks, n0, lane);
+      const FragB b = load_b(AT, 8 * ks, n0, lane);
+      mma3(d0, load_a(AT, 32, 8 * ks, lane), b);
+      mma3(d1, load_a(AT, 48, 8 * ks, lane), b);
     }
     st_tile_f32(AT, 0, 32 + n0, d0, 1.f, lane);
     st_tile_f32(AT, 16, 32 + n0, d1, 1.f, lane);
@@ -187,9 +207,11 @@ __device__ __forceinline__ void solve_merge32(float* AT, int p, int bar) {
   {
     float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) mma_step(d0, AT, 32, 32 + 8 * ks, 8 * ks, 32 + n0, lane);
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) mma_step(d1, AT, 48, 32 + 8 * ks, 8 * ks, 32 + n0, lane);
+    for (int ks = 0; ks < 4; ++ks) {
+      const FragB b = load_b(AT, 8 * ks, 32 + n0, lane);
+      if (ks < 2) mma3(d0, load_a(AT, 32, 32 + 8 * ks, lane), b);
+      mma3(d1, load_a(AT, 48, 32 + 8 * ks, lane), b);
+    }
     st_tile_f32(AT, 32, n0, d0, -1.f, lane);
     st_tile_f32(AT, 48, n0, d1, -1.f, lane);
   }
@@ -314,14 +336,16 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll 2
         for (int j8 = 0; j8 < 8; ++j8) {
           float v[8];
-          tc::tmem_ld8(d0 + j8 * 8, v);
+          tc::tmem_ld8(d0 + j8 * 8, v);  // warp-wide: every lane takes part in the load
           const float4 g0 = *reinterpret_cast<const float4*>(g2 + j8 * 8);
           const float4 g1 = *reinterpret_cast<const float4*>(g2 + j8 * 8 + 4);
           tc::tmem_wait_ld();
           const float gj[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-          float w[8];
+          float w[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (j8 * 8 < t) {  // columns j < t only
 #pragma unroll
-          for (int u = 0; u < 8; ++u) w[u] = j8 * 8 + u < t ? bt * tc::ex2_approx(gt - gj[u]) * v[u] : 0.f;
+            for (int u = 0; u < 8; ++u) w[u] = j8 * 8 + u < t ? bt * tc::ex2_approx(gt - gj[u]) * v[u] : 0.f;
+          }
           *reinterpret_cast<float4*>(AT + t * kLd + j8 * 8) = make_float4(w[0], w[1], w[2], w[3]);
           *reinterpret_cast<float4*>(AT + t * kLd + j8 * 8 + 4) = make_float4(w[4], w[5], w[6], w[7]);
         }
@@ -337,17 +361,21 @@ __global__ void __launch_bounds__(kThreads, 3)
 #pragma unroll 2
       for (int j = gth; j < 512; j += 128) {
         const int r = j >> 3, c8 = (j & 7) ^ (r & 7);
-        const float4 x0 = *reinterpret_cast<const float4*>(AT + r * kLd + c8 * 8);
-        const float4 x1 = *reinterpret_cast<const float4*>(AT + r * kLd + c8 * 8 + 4);
-        float t8[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = hi;
+        if (c8 * 8 <= r) {  // chunks entirely above the diagonal stay zero
+          const float4 x0 = *reinterpret_cast<const float4*>(AT + r * kLd + c8 * 8);
+          const float4 x1 = *reinterpret_cast<const float4*>(AT + r * kLd + c8 * 8 + 4);
+          float t8[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          if (c8 * 8 + 7 > r) {  // the diagonal chunk: zero what lies above the diagonal
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (c8 * 8 + e > r) t8[e] = 0.f;  // above the diagonal (scratch or unwritten)
-        uint4 hi, lo;
-        split2(t8[0], t8[1], hi.x, lo.x);
-        split2(t8[2], t8[3], hi.y, lo.y);
-        split2(t8[4], t8[5], hi.z, lo.z);
-        split2(t8[6], t8[7], hi.w, lo.w);
+            for (int e = 0; e < 8; ++e)
+              if (c8 * 8 + e > r) t8[e] = 0.f;
+          }
+          split2(t8[0], t8[1], hi.x, lo.x);
+          split2(t8[2], t8[3], hi.y, lo.y);
+          split2(t8[4], t8[5], hi.z, lo.z);
+          split2(t8[6], t8[7], hi.w, lo.w);
+        }
         *reinterpret_cast<uint4*>(rec + j * 16) = hi;
         *reinterpret_cast<uint4*>(rec + 8192 + j * 16) = lo;
       }

@@ -167,6 +167,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
       : "memory");
 }
 
+// 8 consecutive 32-bit columns per thread of raw words (packed bf16 pairs).
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // 16 consecutive 32-bit columns per thread of raw words (packed bf16 pairs).
 __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
