@@ -22,6 +22,7 @@ GDN_FLAG_QK_L2NORM = 0x1
 GDN_FLAG_PREFILL_SERIAL = 0x2
 GDN_DEVERR_WAIT_TIMEOUT = 0x1
 GDN_DEVERR_BAD_SEQLENS = 0x2
+GDN_DEVERR_BAD_INDEX = 0x4
 GDN_PREFILL_NOALLOC_SCRATCH_BYTES = 64 << 20
 
 # Every symbol the header declares, with its ctypes signature.
@@ -46,6 +47,15 @@ SIGNATURES = {
                      _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
                      _P, _SZ, _U32, _P], ctypes.c_int),
     "gdn_prefill_workspace_size": ([_I32, _I64, _I32, _I32, _I32, _U32], ctypes.c_size_t),
+    "gdn_decode_pooled": ([_P, _I64, _I64, _I64, _P, _I64, _I64, _I64,   # q, k
+                           _P, _I64, _I64, _I64,                         # v
+                           _P, _I64, _I64, _P, _I32,                     # pool, indices
+                           _P, _P, _I64, _I64, _P, _P, _I64, _I64,       # A_log, a, dt_bias, b
+                           _F,                                           # scale
+                           _P, _I64, _I64, _I64,                         # out
+                           _P, _I64, _I64,                               # new_pool
+                           _P, _I64, _I64, _I64,                         # intermediate
+                           _I32, _I32, _I32, _I32, _I32, _I32, _U32, _P], ctypes.c_int),
     "gdn_prefill_noalloc": ([_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,  # q, k, v
                              _P, _I64, _I64,                                   # state
                              _P, _P, _I64, _P, _P, _I64,                       # A_log, a, dt_bias, b

@@ -182,6 +182,89 @@ size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_
   return gdn::prefill_chunk_workspace_bytes(num_seqs, total_tokens, num_v_heads);
 }
 
+int gdn_decode_pooled(const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+                      int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_b,
+                      int64_t v_stride_t, int64_t v_stride_h, const float* pool, int64_t pool_stride_n,
+                      int64_t pool_stride_h, const void* indices, int32_t indices_is_int64, const float* A_log,
+                      const void* a, int64_t a_stride_b, int64_t a_stride_t, const float* dt_bias, const void* b,
+                      int64_t b_stride_b, int64_t b_stride_t, float scale, void* out, int64_t out_stride_b,
+                      int64_t out_stride_t, int64_t out_stride_h, float* new_pool, int64_t new_pool_stride_n,
+                      int64_t new_pool_stride_h, float* intermediate, int64_t inter_stride_n, int64_t inter_stride_t,
+                      int64_t inter_stride_h, int32_t batch, int32_t tokens, int32_t pool_size, int32_t num_qk_heads,
+                      int32_t num_v_heads, int32_t head_dim, uint32_t flags, void* stream) {
+  int rc = check_common(num_qk_heads, num_v_heads, head_dim);
+  if (rc) return rc;
+  if (batch < 0 || tokens < 0)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "batch and tokens must be >= 0 (got %d, %d)", batch, tokens);
+  if (batch > 65535) return fail(GDN_ERR_UNSUPPORTED, "batch > 65535 per call is not supported (got %d)", batch);
+  if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
+  if (batch == 0 || tokens == 0) return ok();
+  if (pool_size <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "pool_size must be positive (got %d)", pool_size);
+  if (!q || !k || !v || !pool || !indices || !A_log || !a || !dt_bias || !b || !out)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "a required tensor pointer is NULL");
+  if (!aligned(q, q_stride_b, q_stride_h, 2, 8) || !aligned(k, k_stride_b, k_stride_h, 2, 8) ||
+      !aligned(v, v_stride_b, v_stride_h, 2, 8) || (q_stride_t * 2) % 8 || (k_stride_t * 2) % 8)
+    return fail(GDN_ERR_UNSUPPORTED, "q/k/v rows must be 8-byte aligned (base and strides)");
+  rc = check_state_pair(pool, pool_stride_n, pool_stride_h, new_pool, new_pool_stride_n, new_pool_stride_h, pool_size,
+                        num_v_heads);
+  if (rc) return rc;
+  if (intermediate) {
+    if (!aligned(intermediate, inter_stride_n, inter_stride_h, sizeof(float), 16) || (inter_stride_t * 4) % 16)
+      return fail(GDN_ERR_UNSUPPORTED, "intermediate rows must be 16-byte aligned (base and strides)");
+    if (inter_stride_n < 0 || inter_stride_t < 0 || inter_stride_h < 0)
+      return fail(GDN_ERR_INVALID_ARGUMENT, "negative intermediate stride");
+  }
+
+  gdn::DecodeMtpParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.pool = pool;
+  p.new_pool = new_pool;
+  p.indices = indices;
+  p.idx_is_int64 = indices_is_int64 ? 1 : 0;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.inter = intermediate;
+  p.q_sb = q_stride_b;
+  p.q_st = q_stride_t;
+  p.q_sh = q_stride_h;
+  p.k_sb = k_stride_b;
+  p.k_st = k_stride_t;
+  p.k_sh = k_stride_h;
+  p.v_sb = v_stride_b;
+  p.v_st = v_stride_t;
+  p.v_sh = v_stride_h;
+  p.a_sb = a_stride_b;
+  p.a_st = a_stride_t;
+  p.b_sb = b_stride_b;
+  p.b_st = b_stride_t;
+  p.o_sb = out_stride_b;
+  p.o_st = out_stride_t;
+  p.o_sh = out_stride_h;
+  p.s_sn = pool_stride_n;
+  p.s_sh = pool_stride_h;
+  p.n_sn = new_pool_stride_n;
+  p.n_sh = new_pool_stride_h;
+  p.i_sn = inter_stride_n;
+  p.i_st = inter_stride_t;
+  p.i_sh = inter_stride_h;
+  p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim);
+  p.B = batch;
+  p.T = tokens;
+  p.P = pool_size;
+  p.HQ = num_qk_heads;
+  p.HV = num_v_heads;
+  p.ratio = num_v_heads / num_qk_heads;
+  p.flags = flags;
+  const cudaError_t e = gdn::launch_decode_mtp(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_decode_pooled launch");
+  return ok();
+}
+
 int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
                 int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h, const float* state,
                 int64_t state_stride_n, int64_t state_stride_h, const float* A_log, const void* a, int64_t a_stride_t,

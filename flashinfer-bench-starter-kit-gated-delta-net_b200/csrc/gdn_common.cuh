@@ -18,6 +18,7 @@ constexpr int kHeadDim = 128;  // d_k = d_v = 128 (the definition's head size)
 // Device error bits (read by gdn_device_error()).
 constexpr unsigned kDevErrWaitTimeout = 1u << 0;
 constexpr unsigned kDevErrBadSeqlens = 1u << 1;
+constexpr unsigned kDevErrBadIndex = 1u << 2;
 
 // Bounded-wait limit: ~2 s of %globaltimer after the fast spin.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;

@@ -58,7 +58,36 @@ struct PrefillParams {
   size_t workspace_bytes;
 };
 
+// Multi-token decode against a state pool (serving form).  Strides in elements;
+// q, k [B, T, HQ, 128], v [B, T, HV, 128], a, b [B, T, HV], out [B, T, HV, 128],
+// pool / new_pool [P, HV, 128, 128] (rows contiguous), intermediate [P, T, HV, 128, 128].
+struct DecodeMtpParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const float* pool;
+  float* new_pool;  // may equal pool
+  const void* indices;  // [B] int32 or int64 (device)
+  int idx_is_int64;
+  const float* A_log;
+  const __nv_bfloat16* a;
+  const float* dt_bias;
+  const __nv_bfloat16* b;
+  __nv_bfloat16* out;
+  float* inter;  // nullptr: not cached
+  int64_t q_sb, q_st, q_sh, k_sb, k_st, k_sh, v_sb, v_st, v_sh;
+  int64_t a_sb, a_st, b_sb, b_st;
+  int64_t o_sb, o_st, o_sh;
+  int64_t s_sn, s_sh;  // pool
+  int64_t n_sn, n_sh;  // new_pool
+  int64_t i_sn, i_st, i_sh;  // intermediate
+  float scale;
+  int B, T, P, HQ, HV, ratio;
+  uint32_t flags;
+};
+
 int decode_rows_for(int B, int HV);
+cudaError_t launch_decode_mtp(const DecodeMtpParams& p, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeParams& p, int rows, cudaStream_t stream);
 
 cudaError_t launch_prefill_serial(const PrefillParams& p, cudaStream_t stream);

@@ -52,6 +52,7 @@ extern "C" {
 /* Device-side error bits reported by gdn_device_error(). */
 #define GDN_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded wait inside a kernel gave up */
 #define GDN_DEVERR_BAD_SEQLENS 0x2u  /* cu_seqlens not monotone or beyond total_tokens */
+#define GDN_DEVERR_BAD_INDEX 0x4u    /* a state-pool index >= pool_size (gdn_decode_pooled) */
 
 /* Version of this ABI (major * 10000 + minor * 100 + patch). */
 GDN_API int gdn_version(void);
@@ -92,6 +93,44 @@ GDN_API int gdn_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                float* new_state, int64_t new_state_stride_b, int64_t new_state_stride_h,
                int32_t batch, int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
                uint32_t flags, void* stream);
+
+/*
+ * Multi-token decode against a pool of states (the serving form: state slots,
+ * T >= 1 tokens per sequence, e.g. speculative / multi-token prediction).
+ * Follows flashinfer 0.6.11.post2 flashinfer/trace/templates/gdn.py
+ * _gdn_mtp_reference (third party; the reference kit's own decode handles one
+ * token and a dense state batch): sequence b starts from pool[indices[b]], runs
+ * T steps of the decode recurrence of kernel_decode.py:71-103, and writes
+ *   out[b, t]              bf16, every token
+ *   intermediate[s, t]     the state after token t (optional: NULL skips it)
+ *   new_pool[s]            the final state, s = indices[b]
+ * new_pool may alias pool exactly (in-place update; slots no index names are left
+ * as they are); otherwise its other slots are not written.  indices [B] device
+ * int32 (indices_is_int64 = 0) or int64 (= 1), distinct; a negative index skips
+ * the sequence (its outputs are zeros); an index >= pool_size sets
+ * GDN_DEVERR_BAD_INDEX and is skipped.
+ *   q, k       [B, T, num_qk_heads, head_dim]   strides (b, t, h)
+ *   v, out     [B, T, num_v_heads, head_dim]    strides (b, t, h)
+ *   a, b       [B, T, num_v_heads] bf16, head stride 1, strides (b, t)
+ *   pool, new_pool  [pool_size, num_v_heads, head_dim, head_dim] fp32   strides (n, h)
+ *   intermediate    [pool_size, T, num_v_heads, head_dim, head_dim] fp32  strides (n, t, h)
+ */
+GDN_API int gdn_decode_pooled(const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                const void* k, int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                const void* v, int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+                const float* pool, int64_t pool_stride_n, int64_t pool_stride_h,
+                const void* indices, int32_t indices_is_int64,
+                const float* A_log,
+                const void* a, int64_t a_stride_b, int64_t a_stride_t,
+                const float* dt_bias,
+                const void* b, int64_t b_stride_b, int64_t b_stride_t,
+                float scale,
+                void* out, int64_t out_stride_b, int64_t out_stride_t, int64_t out_stride_h,
+                float* new_pool, int64_t new_pool_stride_n, int64_t new_pool_stride_h,
+                float* intermediate, int64_t inter_stride_n, int64_t inter_stride_t, int64_t inter_stride_h,
+                int32_t batch, int32_t tokens, int32_t pool_size,
+                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                uint32_t flags, void* stream);
 
 /*
  * Variable-length prefill.

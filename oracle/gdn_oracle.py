@@ -17,6 +17,8 @@ vectors produced by running those kernels (``tests/golden/make_golden.py``):
                ``kernel_decode.py:115-183`` (default scale ``1/sqrt(d)`` when the
                scale is None or 0, zero state when the state is None, GVA head
                mapping ``qk_head = v_head // (HV // HQ)``).
+* ``decode_pooled`` (multi-token decode against a state pool) follows
+               ``_gdn_mtp_reference`` of the installed flashinfer (third party).
 * ``prefill``  follows ``kernel_prefill.py:42-142`` and its host wrapper
                ``kernel_prefill.py:156-231``: a token-serial decode recurrence
                per (sequence, v-head); an empty sequence passes its initial
@@ -179,27 +181,48 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None, use_qk
 # --------------------------------------------------------------------------
 # pooled-state multi-token decode (serving form)
 # --------------------------------------------------------------------------
-def decode_pooled(q, k, v, pool, indices, A_log, a, dt_bias, b, scale=None, use_qk_l2norm=False):
-    """Multi-token decode against a state pool, updated in place.
+def decode_pooled(q, k, v, pool, indices, A_log, a, dt_bias, b, scale=None, use_qk_l2norm=False,
+                  return_intermediate=False):
+    """Multi-token decode against a state pool (the serving form).
+
+    Follows ``_gdn_mtp_reference`` of ``flashinfer/trace/templates/gdn.py``
+    (flashinfer 0.6.11.post2, third party; the starter kit has no multi-token
+    entry point): sequence i runs the token-serial recurrence of
+    ``kernel_decode.py:83-87`` for T tokens from ``pool[indices[i]]``, writes every
+    token's output and the final state back to that slot.  A negative index skips
+    the sequence and leaves its outputs zero (the serving convention for padded
+    entries; the third-party reference would index from the end of the pool).
 
     q, k ``[B, T, HQ, D]``, v ``[B, T, HV, D]``, a, b ``[B, T, HV]`` (bf16 bits);
-    pool float32 ``[P, HV, D, D]``; indices int ``[B]`` (slot of each sequence;
-    a negative index skips the sequence and leaves its outputs zero).
-    Each sequence runs the same token-serial recurrence as ``prefill`` starting
-    from ``pool[indices[i]]`` and writes its final state back to that slot.
-    Returns (out bf16 bits ``[B, T, HV, D]``, updated pool).
+    pool float32 ``[P, HV, D, D]``; indices int ``[B]``.
+    Returns (out bf16 bits ``[B, T, HV, D]``, updated pool) and, with
+    ``return_intermediate``, also ``{(slot, t): state after token t}``.
     """
     B, T, HQ, D = q.shape
     HV = v.shape[2]
+    scale = default_scale(scale, D)
+    ratio = HV // HQ
     pool = np.array(pool, np.float32, copy=True)
-    out = np.zeros((B, T, HV), np.uint16)[..., None].repeat(D, axis=-1)
+    out = np.zeros((B, T, HV, D), np.float32)
+    inter = {}
     for i in range(B):
         slot = int(indices[i])
         if slot < 0:
             continue
-        cu = np.array([0, T])
-        o, ns = prefill(q[i], k[i], v[i], pool[slot:slot + 1], A_log, a[i], dt_bias, b[i], cu,
-                        scale, use_qk_l2norm)
-        out[i] = o
-        pool[slot] = ns[0]
-    return out, pool
+        qf, kf, vf = bf16_bits_to_f32(q[i]), bf16_bits_to_f32(k[i]), bf16_bits_to_f32(v[i])
+        if use_qk_l2norm:
+            qf, kf = l2norm(qf), l2norm(kf)
+        g, beta = gates(A_log, bf16_bits_to_f32(a[i]), dt_bias, bf16_bits_to_f32(b[i]))
+        S = np.array(pool[slot], np.float32)
+        for t in range(T):
+            qh = np.repeat(qf[t], ratio, axis=0)
+            kh = np.repeat(kf[t], ratio, axis=0)
+            S, out[i, t] = _rows_step(S, kh, qh, vf[t], g[t], beta[t], scale)
+            if return_intermediate:
+                inter[(slot, t)] = S
+        pool[slot] = S
+    outb = f32_to_bf16_bits(out)
+    outb[np.asarray(indices) < 0] = 0
+    if return_intermediate:
+        return outb, pool, inter
+    return outb, pool

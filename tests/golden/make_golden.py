@@ -5,7 +5,8 @@ Runs the reference solution's own Triton kernels
 the CPU under ``TRITON_INTERPRET=1``, plus the definition's torch reference
 recurrence shipped with ``flashinfer==0.6.11.post2``
 (``flashinfer/trace/templates/gdn.py``: ``_gdn_decode_reference``,
-``_gdn_prefill_reference``), on small seeded inputs, and stores inputs and
+``_gdn_prefill_reference``, and ``_gdn_mtp_reference`` for the pooled
+multi-token decode, which the kit itself does not have), on small seeded inputs, and stores inputs and
 outputs as compressed ``.npz`` files (the torch reference's states are kept
 only as their max difference from the Triton kernels' states, to keep the
 fixtures small).  bf16 tensors are stored as uint16 bit
@@ -56,7 +57,7 @@ def main(ref_root: str) -> None:
     sys.path.insert(0, str(Path(ref_root) / "solution" / "triton"))
     import kernel_decode  # reference decode entry point
     import kernel_prefill  # reference prefill entry point
-    from flashinfer.trace.templates.gdn import _gdn_decode_reference, _gdn_prefill_reference
+    from flashinfer.trace.templates.gdn import _gdn_decode_reference, _gdn_mtp_reference, _gdn_prefill_reference
 
     # ---- decode, the reference definition's own head counts (qk4 / v8) ----
     cases = [("decode_qk4v8_b3", 3, 4, 8, 11, True, None),
@@ -99,6 +100,22 @@ def main(ref_root: str) -> None:
           "state (non-empty seqs)", max((s_tr[i] - s_fi[i]).abs().max().item() for i in (0, 2)),
           "empty-seq state: triton passes through", (s_tr[1] - state[1]).abs().max().item(),
           "torch-ref writes zeros", s_fi[1].abs().max().item())
+
+    # ---- multi-token decode against a state pool (flashinfer's _gdn_mtp_reference; the
+    #      reference kit has no multi-token entry point): 2 sequences x 3 tokens, pool of 4 ----
+    B, T, P, HQ, HV = 2, 3, 4, 4, 8
+    q, k, v, a, b, A_log, dt_bias, _ = make_inputs((B, T, HQ, 128), (B, T, HV, 128), (B, T, HV), (1, 1, 1, 1), 31)
+    gen = torch.Generator()
+    gen.manual_seed(32)
+    pool = (torch.randn(P, HV, 128, 128, generator=gen) * 0.05).bfloat16().float()
+    idx = torch.tensor([3, 1], dtype=torch.int32)
+    o_fi, pool_fi = _gdn_mtp_reference(q, k, v, pool, idx, A_log, a, dt_bias, b, None)
+    np.savez_compressed(
+        HERE / "mtp_qk4v8_b2_t3_pool4.npz", q=bits(q), k=bits(k), v=bits(v), a=bits(a), b=bits(b),
+        A_log=A_log.numpy(), dt_bias=dt_bias.numpy(), pool=bits(pool.bfloat16()), indices=idx.numpy(),
+        out_torchref=bits(o_fi), final_used_slots_torchref=pool_fi[idx.long()].numpy())
+    print("mtp: pool slots", idx.tolist(), "untouched slots unchanged:",
+          bool(torch.equal(pool_fi[0], pool[0]) and torch.equal(pool_fi[2], pool[2])))
 
 
 if __name__ == "__main__":

@@ -117,3 +117,22 @@ def test_cpu_tensors_are_rejected(gdn):
     inp = gdn.workloads.decode_inputs(1)
     with pytest.raises(RuntimeError, match="CUDA"):
         gdn.kernel_decode.run(**inp)
+
+
+def test_decode_pooled_rejects_bad_arguments(lib):
+    def call(**over):
+        a = dict(pool=16, idx=8, B=2, T=3, P=4, HQ=16, HV=32, D=128, new_pool=16, out=8, flags=0)
+        a.update(over)
+        return lib.gdn_decode_pooled(8, 3 * 2048, 2048, 128, 8, 3 * 2048, 2048, 128, 8, 3 * 4096, 4096, 128,
+                                     a["pool"], 32 * 16384, 16384, a["idx"], 0,
+                                     16, 8, 96, 32, 16, 8, 96, 32, 0.0,
+                                     a["out"], 3 * 4096, 4096, 128, a["new_pool"], 32 * 16384, 16384,
+                                     None, 0, 0, 0, a["B"], a["T"], a["P"], a["HQ"], a["HV"], a["D"], a["flags"], None)
+    assert call(P=0) == 1 and "pool_size" in lib.gdn_last_error().decode()
+    assert call(idx=None) == 1
+    assert call(new_pool=None) == 1
+    assert call(new_pool=24) == 2  # not 16-byte aligned
+    assert call(pool=16, new_pool=16 + 1024) == 1 and "overlap" in lib.gdn_last_error().decode()
+    assert call(D=64) == 2
+    assert call(flags=0x2) == 1
+    assert call(B=0) == 0 and call(T=0) == 0

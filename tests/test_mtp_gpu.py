@@ -1,0 +1,123 @@
+"""Pooled multi-token decode (``kernel_mtp``, C ABI ``gdn_decode_pooled``) on the GPU
+against flashinfer's ``_gdn_mtp_reference`` fixture and the CPU oracle.
+Tolerances as everywhere: bf16 outputs atol = rtol = 1e-2, states 1e-3 relative."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, state_close
+from oracle import gdn_oracle as ref
+
+pytestmark = pytest.mark.gpu
+OUT_TOL = dict(atol=1e-2, rtol=1e-2)
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def mtp_inputs(gdn, B, T, P, HQ=16, HV=32, seed=0):
+    """B sequences x T tokens in the BASELINE distributions, a pool of P states."""
+    wl = gdn.workloads
+    inp = wl.prefill_inputs([T] * B, num_qk_heads=HQ, num_v_heads=HV, seed=seed)
+    rs = lambda t: t.reshape(B, T, *t.shape[1:])  # noqa: E731
+    gen = torch.Generator().manual_seed(seed + 1)
+    pool = torch.randn(P, HV, 128, 128, generator=gen) * 0.05
+    return dict(q=rs(inp["q"]), k=rs(inp["k"]), v=rs(inp["v"]), a=rs(inp["a"]), b=rs(inp["b"]),
+                A_log=inp["A_log"], dt_bias=inp["dt_bias"], pool=pool)
+
+
+def oracle(d, idx, **kw):
+    return ref.decode_pooled(bits(d["q"]), bits(d["k"]), bits(d["v"]), d["pool"].numpy(), np.asarray(idx),
+                             d["A_log"].numpy(), bits(d["a"]), d["dt_bias"].numpy(), bits(d["b"]), None, **kw)
+
+
+def run_gpu(gdn, d, idx, inter=None, **kw):
+    c = {k: v.cuda() for k, v in d.items()}
+    return gdn.kernel_mtp.run(c["q"], c["k"], c["v"], c["pool"], torch.tensor(idx, device="cuda"), c["A_log"],
+                              c["a"], c["dt_bias"], c["b"], None, inter, **kw)
+
+
+def check(out, pool, o_ref, p_ref):
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref.bf16_bits_to_f32(o_ref), **OUT_TOL)
+    ok, err = state_close(pool.cpu().numpy(), p_ref, 1e-3)
+    assert ok, f"state rel err {err}"
+
+
+def test_golden_flashinfer_mtp_reference(gdn):
+    g = load_golden("mtp_qk4v8_b2_t3_pool4")
+    tb = lambda x: torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).cuda()  # noqa: E731
+    pool = torch.from_numpy(ref.bf16_bits_to_f32(g["pool"])).cuda()
+    idx = torch.from_numpy(g["indices"]).cuda()
+    out, fin = gdn.kernel_mtp.run(tb(g["q"]), tb(g["k"]), tb(g["v"]), pool, idx, torch.from_numpy(g["A_log"]).cuda(),
+                                  tb(g["a"]), torch.from_numpy(g["dt_bias"]).cuda(), tb(g["b"]), None)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref.bf16_bits_to_f32(g["out_torchref"]), **OUT_TOL)
+    ok, err = state_close(fin[idx.long()].cpu().numpy(), g["final_used_slots_torchref"], 1e-3)
+    assert ok, err
+    assert torch.equal(fin[0], pool[0]) and torch.equal(fin[2], pool[2])  # untouched slots
+
+
+@pytest.mark.parametrize("T", [1, 4, 19])  # 19: two token groups of the kernel
+def test_random_pool_with_padding_entry(gdn, T):
+    d = mtp_inputs(gdn, B=5, T=T, P=8, seed=200 + T)
+    idx = [6, -1, 0, 3, 7]
+    out, fin = run_gpu(gdn, d, idx)
+    torch.cuda.synchronize()
+    o_ref, p_ref = oracle(d, idx)
+    check(out, fin, o_ref, p_ref)
+    assert not out[1].float().abs().any()  # the padded entry's outputs are zero
+    assert gdn._lib.device_error() == 0
+
+
+def test_intermediate_states_and_in_place_pool(gdn):
+    B, T, P = 3, 5, 4
+    d = mtp_inputs(gdn, B=B, T=T, P=P, seed=210)
+    idx = [2, 0, 3]
+    o_ref, p_ref, inter_ref = oracle(d, idx, return_intermediate=True)
+    c = {k: v.cuda() for k, v in d.items()}
+    pool = c["pool"].clone()
+    inter = torch.full((P, T, 32, 128, 128), float("nan"), device="cuda")
+    out = torch.empty(B, T, 32, 128, dtype=torch.bfloat16, device="cuda")
+    gdn.kernel_mtp.run_dps(c["q"], c["k"], c["v"], pool, torch.tensor(idx, device="cuda"), c["A_log"], c["a"],
+                           c["dt_bias"], c["b"], None, out, pool, inter)  # in place: final_state is the pool
+    torch.cuda.synchronize()
+    check(out, pool, o_ref, p_ref)
+    for (slot, t), s_ref in inter_ref.items():
+        ok, err = state_close(inter[slot, t].cpu().numpy()[None], s_ref[None], 1e-3)
+        assert ok, (slot, t, err)
+    assert torch.isnan(inter[1]).all()  # slot 1 is not named: its buffer is not written
+
+
+def test_qk_l2norm_and_gva_ratio_4(gdn):
+    d = mtp_inputs(gdn, B=2, T=3, P=3, HQ=8, HV=32, seed=220)
+    d["q"] = (d["q"].float() * 2.0).bfloat16()
+    idx = [1, 2]
+    out, fin = run_gpu(gdn, d, idx, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    o_ref, p_ref = oracle(d, idx, use_qk_l2norm=True)
+    check(out, fin, o_ref, p_ref)
+
+
+def test_one_token_equals_dense_decode(gdn):
+    """T = 1 with indices 0..B-1 is the single-token decode of the dense state batch."""
+    B = 6
+    inp = gdn.workloads.decode_inputs(B, seed=230)
+    c = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in inp.items()}
+    o1, s1 = gdn.kernel_decode.run(**c)
+    o2, s2 = gdn.kernel_mtp.run(c["q"], c["k"], c["v"], c["state"], torch.arange(B, device="cuda"), c["A_log"],
+                                c["a"], c["dt_bias"], c["b"], c["scale"])
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+    assert torch.equal(s1, s2)
+
+
+def test_index_beyond_pool_sets_device_error(gdn):
+    d = mtp_inputs(gdn, B=2, T=2, P=2, seed=240)
+    gdn._lib.device_error(clear=True)
+    out, fin = run_gpu(gdn, d, [0, 5])
+    torch.cuda.synchronize()
+    assert gdn._lib.device_error(clear=True) & gdn._lib.GDN_DEVERR_BAD_INDEX
+    assert not out[1].float().abs().any()

@@ -122,3 +122,18 @@ def test_pooled_decode_oracle_matches_prefill_per_slot(gdn):
         assert np.array_equal(new_pool[slot], s[0])
     for slot in (0, 2, 3):
         assert np.array_equal(new_pool[slot], pool[slot])
+
+
+def test_mtp_oracle_matches_flashinfer_reference():
+    """Pooled multi-token decode: the oracle against flashinfer's ``_gdn_mtp_reference``
+    (the definition-level reference of the serving form; fixture by make_golden.py)."""
+    g = load_golden("mtp_qk4v8_b2_t3_pool4")
+    pool = ref.bf16_bits_to_f32(g["pool"])
+    out, new_pool = ref.decode_pooled(g["q"], g["k"], g["v"], pool, g["indices"], g["A_log"], g["a"],
+                                      g["dt_bias"], g["b"], None)
+    d, m = _ulp_diff(out, g["out_torchref"])
+    assert d <= 2.0 ** -7 * max(m, 1e-3)
+    ok, err = state_close(new_pool[g["indices"]], g["final_used_slots_torchref"], rtol=1e-5)
+    assert ok, err
+    untouched = [s for s in range(pool.shape[0]) if s not in set(g["indices"].tolist())]
+    assert all(np.array_equal(new_pool[s], pool[s]) for s in untouched)
