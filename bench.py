@@ -1,7 +1,7 @@
 """Benchmark of the GDN hot path (driver contract: one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode_b64|decode_b1024|prefill_varlen16|prefill_8x32768]
+                    [--workload decode_b64|decode_b1024|prefill_varlen16|prefill_8x32768|mtp_b64_t4]
 
 Headline (``value``): GDN decode state GB/s on configs[1] (B = 64 sequences,
 16 q/k heads, 32 v heads, d = 128, fp32 k-last state) per GPU; with N GPUs
@@ -11,7 +11,8 @@ one decode call over the batch; inputs are resident in HBM and rotate over
 several buffer sets whose footprint exceeds 3x L2 (126 MB), so no step reads
 L2-resident state.  ``e2e`` times the public ``run()`` with host (pinned)
 inputs and outputs, copies included.  ``prefill`` reports configs[3] (varlen,
-16 sequences) tokens/s on the same ranks.
+16 sequences) tokens/s on the same ranks, ``mtp`` the pooled multi-token decode
+(64 sequences x 4 tokens, in-place state pool) GB/s against the HBM roofline.
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 C restatement in ``oracle/``, all host threads) on a bounded sample of the
@@ -186,6 +187,30 @@ def prefill_call(gdn, s):
                                s["b"], s["cu_seqlens"], s["scale"], s["output"], s["new_state"])
 
 
+def mtp_sets(gdn, batch, tokens, n_sets, seed, device):
+    """Pooled multi-token decode: one state pool of batch * n_sets slots (in-place
+    serving update), n_sets disjoint index sets so consecutive steps touch
+    different slots (pool > 3x L2)."""
+    P = batch * n_sets
+    gen = torch.Generator().manual_seed(seed)
+    pool = (torch.randn(P, 32, 128, 128, generator=gen) * 0.05).to(device)
+    perm = torch.randperm(P, generator=gen)
+    sets = []
+    for i in range(n_sets):
+        inp = gdn.workloads.prefill_inputs([tokens] * batch, seed=seed + 1000 * i, device=device)
+        rs = lambda t: t.reshape(batch, tokens, *t.shape[1:])  # noqa: E731
+        sets.append(dict(q=rs(inp["q"]), k=rs(inp["k"]), v=rs(inp["v"]), a=rs(inp["a"]), b=rs(inp["b"]),
+                         A_log=inp["A_log"], dt_bias=inp["dt_bias"], pool=pool,
+                         idx=perm[i * batch:(i + 1) * batch].to(device=device, dtype=torch.int32),
+                         output=torch.empty(batch, tokens, 32, 128, dtype=torch.bfloat16, device=device)))
+    return sets
+
+
+def mtp_call(gdn, s):
+    gdn.kernel_mtp.run_dps(s["q"], s["k"], s["v"], s["pool"], s["idx"], s["A_log"], s["a"], s["dt_bias"], s["b"],
+                           None, s["output"], s["pool"])
+
+
 def set_bytes(s):
     return sum(v.numel() * v.element_size() for v in s.values() if torch.is_tensor(v))
 
@@ -306,6 +331,32 @@ def cpu_prefill_rate(gdn, seqlens, budget_s, nthreads=None):
         prefix *= 2
 
 
+def cpu_mtp_rate(gdn, batch, tokens, budget_s, nthreads=None):
+    """State GB/s of the C restatement on the pooled multi-token decode: each
+    sequence is ``tokens`` steps of the recurrence from its slot (run as a varlen
+    prefill of ``batch`` sequences of ``tokens`` tokens, which is the same
+    arithmetic); returns (GB/s, sample description, cores)."""
+    import numpy as np
+
+    from oracle import c_oracle
+
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    cores = nthreads or c_oracle.default_threads()
+    inp = gdn.workloads.prefill_inputs([tokens] * batch, seed=0)
+    args = (bits(inp["q"]), bits(inp["k"]), bits(inp["v"]), inp["state"].numpy(), inp["A_log"].numpy(),
+            bits(inp["a"]), inp["dt_bias"].numpy(), bits(inp["b"]), inp["cu_seqlens"].numpy(), inp["scale"])
+    c_oracle.prefill(*args, nthreads=cores)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        c_oracle.prefill(*args, nthreads=cores)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    gb = gdn.workloads.mtp_bytes_per_seq(tokens) * batch * reps / 1e9
+    return gb / el, f"{reps} calls of B={batch} x T={tokens} tokens (16/32 heads) in {el:.1f} s", cores
+
+
 # ----------------------------------------------------------------------------- main
 def run_reference(args, world, rank):
     """Reference arm: the reference algorithm's CPU implementation (the C
@@ -397,7 +448,32 @@ def run_ours(args, world, rank, local):
             gpu_launches=args.steps,
             clocks=sampler.summary())
         del sets
-    if args.prefill and not wl.startswith("prefill"):
+    if wl.startswith("decode") or wl == "mtp_b64_t4":
+        # pooled multi-token decode (serving form): 64 sequences x 4 tokens per call, in place
+        mb, mt = 64, 4
+        msets = mtp_sets(gdn, mb, mt, 3, seed=rank + 7, device="cuda")
+        msteps = args.steps if wl == "mtp_b64_t4" else max(20, min(200, args.steps // 10))
+        mwarm = args.warmup if wl == "mtp_b64_t4" else 5
+        sampler_m = ClockSampler(local) if wl == "mtp_b64_t4" else None
+        mms, mlaunch = time_steps(lambda s: mtp_call(gdn, s), msets, msteps, mwarm, world, sampler_m)
+        mbytes = gdn.workloads.mtp_bytes_per_seq(mt) * mb
+        mres = {"workload": "mtp_b64_t4", "gbs": sum_over_ranks(mbytes, world) / (mms * 1e-3) / 1e9,
+                "tokens_per_s": sum_over_ranks(mb * mt, world) / (mms * 1e-3), "ms_per_step": mms,
+                "roofline": {"bound": "hbm", "achieved": mbytes / (mlaunch * 1e-3) / 1e9, "peak": hbm_peak,
+                             "unit": "GB/s", "frac": mbytes / (mlaunch * 1e-3) / 1e9 / hbm_peak,
+                             "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)", "kernel": "decode_mtp_kernel",
+                             "avg_launch_us": mlaunch * 1e3, "algorithmic_bytes_per_launch": mbytes}}
+        if wl == "mtp_b64_t4":
+            result.update(metric="GDN multi-token decode state GB/s", value=mres["gbs"], unit="GB/s",
+                          ms_per_step=mms, dtype="f32",
+                          config={"workload": wl, "batch_per_rank": mb, "tokens_per_seq": mt,
+                                  "pool_slots": 3 * mb, "l2": "3 disjoint slot sets, 805 MB pool",
+                                  "parallelism": f"dp{world}"},
+                          roofline=mres["roofline"], gpu_launches=msteps, clocks=sampler_m.summary(), e2e=None)
+        else:
+            result["mtp"] = mres
+        del msets
+    if args.prefill and not wl.startswith("prefill") and wl != "mtp_b64_t4":
         wl_p = "prefill_varlen16"
     elif wl.startswith("prefill"):
         wl_p = wl
@@ -442,6 +518,10 @@ def run_ours(args, world, rank, local):
                 v, sample, cores = cpu_decode_rate(gdn, 64 if wl == "decode_b64" else 1024, budget)
                 result["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
                                           "sample": sample}
+            elif wl == "mtp_b64_t4":
+                v, sample, cores = cpu_mtp_rate(gdn, 64, 4, budget)
+                result["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
+                                          "sample": sample}
             else:
                 v, sample, cores = cpu_prefill_rate(gdn, seqlens, budget)
                 result["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
@@ -461,7 +541,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_b64",
-                    choices=["decode_b64", "decode_b1024", "prefill_varlen16", "prefill_8x32768"])
+                    choices=["decode_b64", "decode_b1024", "prefill_varlen16", "prefill_8x32768", "mtp_b64_t4"])
     ap.add_argument("--no-prefill", dest="prefill", action="store_false",
                     help="skip the secondary configs[3] prefill measurement")
     args = ap.parse_args()

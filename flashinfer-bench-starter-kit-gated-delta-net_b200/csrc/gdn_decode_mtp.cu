@@ -12,10 +12,15 @@
 //
 // Design: as the single-token kernel (CTA = 4 warps owning ROWS state rows of one
 // (sequence, v-head); rows arrive by 1-D bulk copies, one mbarrier per warp
-// slice), but the rows stay in registers (a lane holds 4 consecutive K
-// elements of each of its warp's rows) for all T tokens, so the state crosses
-// HBM once per call.  q, k, v and the gates of up to kTokGroup tokens are
-// staged in shared memory (fp32) per group, so the per-token loads overlap.
+// slice), but the rows stay in registers for all T tokens, so the state crosses
+// HBM once per call.  Eight lanes share a row: lane c of the eight holds K
+// elements 32 j + 4 c .. 32 j + 4 c + 3 (j = 0..3), so the eight lanes' 16-byte
+// accesses cover 128 contiguous bytes.  A warp thus works on 4 rows at once and
+// each dot product needs a 3-level shuffle reduction; the decay is folded in
+// (S.k and S.q are taken on the undecayed row and scaled by g).  The row math
+// runs on packed fp32x2 instructions (__ffma2_rn / __fmul2_rn / __fadd2_rn), two
+// columns per instruction.  q, k, v and the gates of up to kTokGroup tokens are
+// staged in shared memory (fp32) per group.
 #include "gdn_common.cuh"
 #include "gdn_kernels.h"
 
@@ -84,9 +89,11 @@ __global__ void __launch_bounds__(128) decode_mtp_kernel(DecodeMtpParams p) {
 
   const int qh = h / p.ratio;
   const float A_log = p.A_log[h], dt_bias = p.dt_bias[h], scale = p.scale;
-  float4 s[R];  // this lane's 4 columns of each of the warp's rows
+  constexpr int kPasses = R / 4;                      // rows per lane
+  static_assert(R % 4 == 0, "four rows per warp pass");
+  const int rg = lane >> 3, cs = lane & 7;             // row in the pass, column slice
+  float2 s[kPasses][8];  // s[ps][2 j + e]: columns 32 j + 4 cs + 2 e, + 1 of row ps * 4 + rg
   bool have_rows = false, rows_ok = true;
-  float* dst = p.new_pool + (size_t)slot * p.n_sn + (size_t)h * p.n_sh + (size_t)wrow0 * kHeadDim + lane * 4;
 
   for (int tg = 0; tg < p.T; tg += kTokGroup) {
     const int nt = min(kTokGroup, p.T - tg);
@@ -116,63 +123,105 @@ __global__ void __launch_bounds__(128) decode_mtp_kernel(DecodeMtpParams p) {
       // a timed-out copy (recorded by mbar_wait) leaves this warp without rows: it
       // keeps taking part in the CTA barriers but computes and stores nothing
       rows_ok = mbar_wait(&bars[warp], 0);
-      const float* wtile = tile + warp * R * kHeadDim;
 #pragma unroll
-      for (int r = 0; r < R; ++r)
-        s[r] = rows_ok ? *reinterpret_cast<const float4*>(wtile + r * kHeadDim + lane * 4)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int ps = 0; ps < kPasses; ++ps) {
+        const float* src = tile + (warp * R + ps * 4 + rg) * kHeadDim + cs * 4;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const float4 x = rows_ok ? *reinterpret_cast<const float4*>(src + c4 * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+          s[ps][2 * c4] = make_float2(x.x, x.y);
+          s[ps][2 * c4 + 1] = make_float2(x.z, x.w);
+        }
+      }
       have_rows = true;
     }
     if (!rows_ok) continue;
-    // ---- nt sequential decode steps on the register-resident rows ----
+    // ---- nt sequential decode steps on the register-resident rows (packed fp32x2 math) ----
 #pragma unroll 1
     for (int t = 0; t < nt; ++t) {
-      float4 kv = *reinterpret_cast<const float4*>(sqk + (t * 2 + 1) * kHeadDim + lane * 4);
-      float4 qv = *reinterpret_cast<const float4*>(sqk + (t * 2) * kHeadDim + lane * 4);
+      float2 kv[8], qv[8];
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(sqk + (t * 2 + 1) * kHeadDim + cs * 4 + c4 * 32);
+        const float4 q4 = *reinterpret_cast<const float4*>(sqk + (t * 2) * kHeadDim + cs * 4 + c4 * 32);
+        kv[2 * c4] = make_float2(k4.x, k4.y);
+        kv[2 * c4 + 1] = make_float2(k4.z, k4.w);
+        qv[2 * c4] = make_float2(q4.x, q4.y);
+        qv[2 * c4 + 1] = make_float2(q4.z, q4.w);
+      }
+      // k.q (and |k|^2, |q|^2) over the row's 8 lanes (every 8-lane group holds all 128 elements)
+      float2 akq = make_float2(0.f, 0.f), akk = akq, aqq = akq;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        akq = __ffma2_rn(kv[c], qv[c], akq);
+        if (L2NORM) {
+          akk = __ffma2_rn(kv[c], kv[c], akk);
+          aqq = __ffma2_rn(qv[c], qv[c], aqq);
+        }
+      }
+      float kq = akq.x + akq.y;
+      float2 nrm = __fadd2_rn(make_float2(akk.x, aqq.x), make_float2(akk.y, aqq.y));
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        kq += __shfl_xor_sync(0xffffffffu, kq, o);
+        if (L2NORM)
+          nrm = __fadd2_rn(nrm, make_float2(__shfl_xor_sync(0xffffffffu, nrm.x, o),
+                                            __shfl_xor_sync(0xffffffffu, nrm.y, o)));
+      }
       if (L2NORM) {
-        float kk = dot4(kv, kv), qq = dot4(qv, qv);
-        warp_sum2(kk, qq);
-        const float rk = rsqrtf(kk + 1e-6f), rq = rsqrtf(qq + 1e-6f);
-        kv = make_float4(kv.x * rk, kv.y * rk, kv.z * rk, kv.w * rk);
-        qv = make_float4(qv.x * rq, qv.y * rq, qv.z * rq, qv.w * rq);
+        const float rk = rsqrtf(nrm.x + 1e-6f), rq = rsqrtf(nrm.y + 1e-6f);
+        const float2 rk2 = make_float2(rk, rk), rq2 = make_float2(rq, rq);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          kv[c] = __fmul2_rn(kv[c], rk2);
+          qv[c] = __fmul2_rn(qv[c], rq2);
+        }
+        kq *= rk * rq;
       }
-      float kq = dot4(kv, qv);
-      kq = warp_sum(kq);
       const float g = sg[t * 2], beta = sg[t * 2 + 1];
-      const float v_mine = lane < R ? sv[t * ROWS + warp * R + lane] : 0.f;
-      float o_mine = 0.f;
+      const float2 g2 = make_float2(g, g);
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        float4 x = s[r];
-        x.x *= g;
-        x.y *= g;
-        x.z *= g;
-        x.w *= g;
-        float pk = dot4(x, kv), pq = dot4(x, qv);
-        warp_sum2(pk, pq);
-        const float vr = __shfl_sync(0xffffffffu, v_mine, r);
-        const float delta = beta * (vr - pk);
-        x.x = fmaf(delta, kv.x, x.x);
-        x.y = fmaf(delta, kv.y, x.y);
-        x.z = fmaf(delta, kv.z, x.z);
-        x.w = fmaf(delta, kv.w, x.w);
-        s[r] = x;
-        if (lane == r) o_mine = scale * fmaf(delta, kq, pq);
-      }
-      if (lane < R)
-        p.out[(size_t)bi * p.o_sb + (size_t)(tg + t) * p.o_st + (size_t)h * p.o_sh + wrow0 + lane] =
-            __float2bfloat16_rn(o_mine);
-      if (p.inter) {
-        float* idst = p.inter + (size_t)slot * p.i_sn + (size_t)(tg + t) * p.i_st + (size_t)h * p.i_sh +
-                      (size_t)wrow0 * kHeadDim + lane * 4;
+      for (int ps = 0; ps < kPasses; ++ps) {
+        const int r = ps * 4 + rg;  // row within the warp
+        float2 ak = make_float2(0.f, 0.f), aq = ak;  // S.k, S.q on the undecayed row
 #pragma unroll
-        for (int r = 0; r < R; ++r) st_cs_f4(idst + r * kHeadDim, s[r]);
+        for (int c = 0; c < 8; ++c) {
+          ak = __ffma2_rn(s[ps][c], kv[c], ak);
+          aq = __ffma2_rn(s[ps][c], qv[c], aq);
+        }
+        float2 pkq = __fadd2_rn(make_float2(ak.x, aq.x), make_float2(ak.y, aq.y));
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1)
+          pkq = __fadd2_rn(pkq, make_float2(__shfl_xor_sync(0xffffffffu, pkq.x, o),
+                                            __shfl_xor_sync(0xffffffffu, pkq.y, o)));
+        const float delta = beta * (sv[t * ROWS + warp * R + r] - g * pkq.x);
+        const float2 d2 = make_float2(delta, delta);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) s[ps][c] = __ffma2_rn(g2, s[ps][c], __fmul2_rn(d2, kv[c]));
+        if (cs == 0)
+          p.out[(size_t)bi * p.o_sb + (size_t)(tg + t) * p.o_st + (size_t)h * p.o_sh + wrow0 + r] =
+              __float2bfloat16_rn(scale * fmaf(delta, kq, g * pkq.y));
+        if (p.inter) {
+          float* idst = p.inter + (size_t)slot * p.i_sn + (size_t)(tg + t) * p.i_st + (size_t)h * p.i_sh +
+                        (size_t)(wrow0 + r) * kHeadDim + cs * 4;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            st_cs_f4(idst + c4 * 32, make_float4(s[ps][2 * c4].x, s[ps][2 * c4].y, s[ps][2 * c4 + 1].x,
+                                                 s[ps][2 * c4 + 1].y));
+        }
       }
     }
   }
   if (rows_ok) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) st_cs_f4(dst + r * kHeadDim, s[r]);
+    for (int ps = 0; ps < kPasses; ++ps) {
+      float* dst = p.new_pool + (size_t)slot * p.n_sn + (size_t)h * p.n_sh +
+                   (size_t)(wrow0 + ps * 4 + rg) * kHeadDim + cs * 4;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4)
+        st_cs_f4(dst + c4 * 32, make_float4(s[ps][2 * c4].x, s[ps][2 * c4].y, s[ps][2 * c4 + 1].x,
+                                            s[ps][2 * c4 + 1].y));
+    }
   }
 }
 

@@ -136,6 +136,14 @@ def decode_bytes_per_seq(num_qk_heads=NUM_QK_HEADS, num_v_heads=NUM_V_HEADS, d=H
             + num_v_heads * 2 * 2)
 
 
+def mtp_bytes_per_seq(tokens, num_qk_heads=NUM_QK_HEADS, num_v_heads=NUM_V_HEADS, d=HEAD_DIM) -> int:
+    """Pooled multi-token decode, one sequence: its state slot read + written once
+    (fp32) plus q, k, v, o (bf16) and a, b (bf16) of every token (no intermediate
+    states cached)."""
+    return (num_v_heads * d * d * 4 * 2
+            + tokens * (num_qk_heads * d * 2 * 2 + num_v_heads * d * 2 * 2 + num_v_heads * 2 * 2))
+
+
 def prefill_flops_per_token(num_v_heads=NUM_V_HEADS, d=HEAD_DIM, chunk=64) -> float:
     """Chunked WY/UT FLOPs per token: HV * (10*C*d + 6*d^2 + (2/3)*C^2)."""
     return num_v_heads * (10 * chunk * d + 6 * d * d + (2.0 / 3.0) * chunk * chunk)

@@ -102,7 +102,11 @@ def test_qk_l2norm_and_gva_ratio_4(gdn):
 
 
 def test_one_token_equals_dense_decode(gdn):
-    """T = 1 with indices 0..B-1 is the single-token decode of the dense state batch."""
+    """T = 1 with indices 0..B-1 is the single-token decode of the dense state batch,
+    up to fp32 rounding: the pooled kernel reduces over 8 lanes per row and takes
+    S.k on the undecayed row (g (S.k) instead of (g S).k), the dense one over 32
+    lanes on the decayed row.  States agree to 1e-6 absolute (entries ~0.05),
+    outputs to one bf16 ulp."""
     B = 6
     inp = gdn.workloads.decode_inputs(B, seed=230)
     c = {k: (v.cuda() if torch.is_tensor(v) else v) for k, v in inp.items()}
@@ -110,8 +114,8 @@ def test_one_token_equals_dense_decode(gdn):
     o2, s2 = gdn.kernel_mtp.run(c["q"], c["k"], c["v"], c["state"], torch.arange(B, device="cuda"), c["A_log"],
                                 c["a"], c["dt_bias"], c["b"], c["scale"])
     torch.cuda.synchronize()
-    assert torch.equal(o1, o2)
-    assert torch.equal(s1, s2)
+    torch.testing.assert_close(s2, s1, atol=1e-6, rtol=0)
+    torch.testing.assert_close(o2.float(), o1.float(), atol=1e-3, rtol=2 ** -7)
 
 
 def test_index_beyond_pool_sets_device_error(gdn):
