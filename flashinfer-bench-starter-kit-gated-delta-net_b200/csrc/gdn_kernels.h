@@ -84,6 +84,8 @@ struct DecodeMtpParams {
   float scale;
   int B, T, P, HQ, HV, ratio;
   uint32_t flags;
+  uint32_t hv_mul;  // n / HV = (umulhi(n, hv_mul) + n) >> hv_shr for n < 2^31 (set by the launcher)
+  int hv_shr;
 };
 
 int decode_rows_for(int B, int HV);

@@ -60,7 +60,7 @@ def test_golden_flashinfer_mtp_reference(gdn):
     assert torch.equal(fin[0], pool[0]) and torch.equal(fin[2], pool[2])  # untouched slots
 
 
-@pytest.mark.parametrize("T", [1, 4, 19])  # 19: two token groups of the kernel
+@pytest.mark.parametrize("T", [1, 4, 8, 19])  # <= 8: warp-pipelined kernel; 19: two token groups
 def test_random_pool_with_padding_entry(gdn, T):
     d = mtp_inputs(gdn, B=5, T=T, P=8, seed=200 + T)
     idx = [6, -1, 0, 3, 7]
@@ -70,6 +70,44 @@ def test_random_pool_with_padding_entry(gdn, T):
     check(out, fin, o_ref, p_ref)
     assert not out[1].float().abs().any()  # the padded entry's outputs are zero
     assert gdn._lib.device_error() == 0
+
+
+def test_many_items_per_warp(gdn):
+    """160 sequences = 81,920 eight-row items, several per warp of the persistent
+    grid, so every warp cycles both stages of its copy pipeline; padded entries
+    interleaved."""
+    B, T, P = 160, 2, 170
+    d = mtp_inputs(gdn, B=B, T=T, P=P, HQ=16, HV=32, seed=215)
+    idx = list(np.random.default_rng(215).permutation(P)[:B])
+    idx[7] = idx[100] = -1
+    out, fin = run_gpu(gdn, d, idx)
+    torch.cuda.synchronize()
+    o_ref, p_ref = oracle(d, idx)
+    check(out, fin, o_ref, p_ref)
+    assert gdn._lib.device_error() == 0
+
+
+@pytest.mark.parametrize("T", [3, 8])
+def test_rows_on_8_byte_boundaries(gdn, T):
+    """q/k/v rows 8-byte but not 16-byte aligned (head stride 132 elements): the
+    general kernel runs instead of the bulk-copy pipeline, same results."""
+    B, P = 4, 6
+    d = mtp_inputs(gdn, B=B, T=T, P=P, seed=216 + T)
+    idx = [5, 0, -1, 2]
+    o_ref, p_ref = oracle(d, idx)
+    c = {k: v.cuda() for k, v in d.items()}
+
+    def pad(x):  # same values, rows starting 4 elements (8 bytes) into a 132-wide buffer
+        big = torch.zeros(*x.shape[:-1], 132, dtype=x.dtype, device=x.device)
+        big[..., 4:] = x
+        return big[..., 4:]
+
+    q, k, v = pad(c["q"]), pad(c["k"]), pad(c["v"])
+    assert q.stride(2) == 132 and q.data_ptr() % 16 == 8
+    out, fin = gdn.kernel_mtp.run(q, k, v, c["pool"], torch.tensor(idx, device="cuda"), c["A_log"], c["a"],
+                                  c["dt_bias"], c["b"], None)
+    torch.cuda.synchronize()
+    check(out, fin, o_ref, p_ref)
 
 
 def test_intermediate_states_and_in_place_pool(gdn):
