@@ -20,6 +20,12 @@ GDN_ERR_CUDA = 3
 GDN_ERR_WORKSPACE = 4
 GDN_FLAG_QK_L2NORM = 0x1
 GDN_FLAG_PREFILL_SERIAL = 0x2
+
+
+def GDN_PREFILL_SEGMENTS(n: int) -> int:
+    """Flag bits requesting n context-parallel segments per sequence (0 = automatic, 1 = none)."""
+    return (int(n) & 15) << 8
+
 GDN_DEVERR_WAIT_TIMEOUT = 0x1
 GDN_DEVERR_BAD_SEQLENS = 0x2
 GDN_DEVERR_BAD_INDEX = 0x4

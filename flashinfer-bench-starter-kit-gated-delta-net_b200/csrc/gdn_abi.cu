@@ -179,7 +179,7 @@ size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_
   // the token-serial kernel (forced, or for in-kernel q/k normalisation) needs none;
   // the chunked kernel keeps one prepared record per chunk slot and v-head
   if (flags & (GDN_FLAG_PREFILL_SERIAL | GDN_FLAG_QK_L2NORM)) return 0;
-  return gdn::prefill_chunk_workspace_bytes(num_seqs, total_tokens, num_v_heads);
+  return gdn::prefill_chunk_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
 }
 
 int gdn_decode_pooled(const void* q, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, const void* k,
@@ -279,7 +279,7 @@ int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const voi
     return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0 (got %d, %lld)", num_seqs,
                 (long long)total_tokens);
   if (num_seqs > 65535) return fail(GDN_ERR_UNSUPPORTED, "num_seqs > 65535 per call is not supported");
-  if (flags & ~(GDN_FLAG_QK_L2NORM | GDN_FLAG_PREFILL_SERIAL))
+  if (flags & ~(GDN_FLAG_QK_L2NORM | GDN_FLAG_PREFILL_SERIAL | GDN_PREFILL_SEGMENTS(15)))
     return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
   if (num_seqs == 0) return ok();
   if (!cu_seqlens) return fail(GDN_ERR_INVALID_ARGUMENT, "cu_seqlens must not be NULL");

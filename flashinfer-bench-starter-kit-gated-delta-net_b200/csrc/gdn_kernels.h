@@ -56,6 +56,12 @@ struct PrefillParams {
   uint32_t flags;
   void* workspace;
   size_t workspace_bytes;
+  // context parallelism inside the GPU (set by the chunked launcher): each sequence's
+  // chunks split into cp_segments ranges; cp_pass 0 = one chain per sequence, 1 = the
+  // segment maps, 3 = the segment reruns; cp_scratch = segment states and maps
+  int cp_segments = 1;
+  int cp_pass = 0;
+  float* cp_scratch = nullptr;
 };
 
 // Multi-token decode against a state pool (serving form).  Strides in elements;
@@ -97,7 +103,11 @@ cudaError_t launch_prefill_serial(const PrefillParams& p, cudaStream_t stream);
 // Chunked tensor-core prefill: usable when q/k/v rows and strides are 16-byte
 // aligned (TMA), no in-kernel q/k normalisation is requested and the workspace
 // holds prefill_chunk_workspace_bytes (one record per chunk slot and v-head).
-size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads);
+size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
+// Segments per sequence the chunked prefill uses for this problem (1 = none):
+// flags bits kPrefillSegmentsShift .. + 3 request a count (0 = automatic).
+constexpr int kPrefillSegmentsShift = 8;
+int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
 bool prefill_chunk_supported(const PrefillParams& p);
 cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream);
 

@@ -189,12 +189,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qh = h / p.ratio;
 
-  const int64_t t0 = load_cu(p, n), t1 = load_cu(p, n + 1);
-  const bool bad = t1 < t0 || t0 < 0 || t1 > p.T;
-  const int64_t len = bad ? 0 : t1 - t0;
-  const int nchunks = (int)((len + kC - 1) / kC);
-  if (bad && tid == 0) raise_device_error(kDevErrBadSeqlens);
-  const int64_t slot0 = slot_start(t0, n);  // workspace record slot of chunk 0
+  const int64_t cu0 = load_cu(p, n), cu1 = load_cu(p, n + 1);
+  const bool bad = cu1 < cu0 || cu0 < 0 || cu1 > p.T;
+  if (bad && tid == 0 && blockIdx.z == 0) raise_device_error(kDevErrBadSeqlens);
+  const int64_t seq_len = bad ? 0 : cu1 - cu0;
+
+  // ---- this CTA's task: a chunk range of the sequence, where its state starts and ends ----
+  // cp_pass 0: the whole sequence from p.state to p.new_state, with outputs.
+  // cp_pass 1 (z): 0 = segment 0 from p.state, with outputs, its final state -> kCpIn[0];
+  //   2 s - 1 = M of segment s (identity start, v taken as 0), 2 s = C of segment s
+  //   (zero start), no outputs (s = 1 .. S - 2).
+  // cp_pass 3 (z): segment z + 1 from kCpIn[z], with outputs; the last one ends in p.new_state.
+  const int S = p.cp_segments, cz = blockIdx.z;
+  const int seg = p.cp_pass == 1 ? (cz + 1) >> 1 : (p.cp_pass == 3 ? cz + 1 : 0);
+  const bool emit = p.cp_pass != 1 || cz == 0;          // outputs of the range are written
+  const bool homog = p.cp_pass == 1 && (cz & 1);        // identity start, v taken as 0 (an M)
+  // where the range's state starts (nullptr: zero, or the identity when homog) and ends
+  // (nullptr: not stored); evaluated where used, to keep them out of the loops' registers
+  auto init_block = [&]() -> const float* {
+    if (p.cp_pass == 3) return p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, seg - 1, h);
+    if (p.cp_pass == 1 && cz != 0) return nullptr;
+    return p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh : nullptr;
+  };
+  auto final_block = [&]() -> float* {
+    if (p.cp_pass == 1)
+      return p.cp_scratch + (cz == 0 ? cp_offset(p.N, p.HV, S, kCpIn, n, 0, h)
+                                     : cp_offset(p.N, p.HV, S, (cz & 1) ? kCpMap : kCpOff, n, seg - 1, h));
+    if (p.cp_pass == 3 && seg != S - 1) return nullptr;
+    return p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh;
+  };
+  const int nch_seq = (int)((seq_len + kC - 1) / kC);
+  const int cb = (int)((int64_t)seg * nch_seq / S), ce = (int)((int64_t)(seg + 1) * nch_seq / S);
+  const int64_t t0 = cu0 + (int64_t)cb * kC;  // first token of the range
+  const int64_t len = ce > cb ? (seq_len < (int64_t)ce * kC ? seq_len : (int64_t)ce * kC) - (int64_t)cb * kC : 0;
+  const int nchunks = ce - cb;
+  const int64_t slot0 = slot_start(cu0, n) + cb;  // workspace record slot of the range's chunk 0
 
   if (tid == 0) {
     for (int i = 0; i < B_COUNT; ++i) mbar_init(sm.bar(i), (i == B_GFREE || i == B_GFREE + 1) ? 2 : 1);
@@ -364,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp == kWarpP0) tc::bulk_wait_read_all();  // the previous chunk's row stores have read the stage
       named_sync(2, 128);
 #pragma unroll 1
-      for (int q16 = 0; q16 < 4; ++q16) {
+      for (int q16 = 0; q16 < (emit ? 4 : 0); ++q16) {
         float x[16];
         tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, kTmD1 + (uint32_t)(ci & 1) * 128 + q16 * 16), x);
         tc::tmem_wait_ld();
@@ -375,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_proxy_async_smem();
       named_sync(2, 128);
       if (pleader) mbar_arrive(sm.bar(B_OUT_DONE + (ci & 1)));
-      if (warp == kWarpP0) {
+      if (warp == kWarpP0 && emit) {
         if (nvalid == kC) {  // whole chunk: one tiled store of the [64 x 128] box
           if (lane == 0) tc::tma_store_3d(&mapO, 0, h, (int)(t0 + (int64_t)ci * kC), ostage);
         } else {  // a sequence's last, partial chunk: only its own rows
@@ -490,10 +519,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = tid == 0;
     const int sc = hsel * kStateCols;  // this thread's state columns [sc, sc + kStateCols)
     const int tb = hsel * kTokCols;    // this thread's token columns [tb, tb + kTokCols)
-    // initial state (this thread's columns) -> TMEM S
+    // initial state (this thread's columns) -> TMEM S: loaded, zero or the identity
     {
-      const float* src =
-          p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh + (size_t)v * kHeadDim + sc : nullptr;
+      const float* init_blk = init_block();
+      const float* src = init_blk ? init_blk + (size_t)v * kHeadDim + sc : nullptr;
 #pragma unroll
       for (int c0 = 0; c0 < kStateCols; c0 += 16) {
         float x[16];
@@ -504,6 +533,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           x[q + 1] = f.y;
           x[q + 2] = f.z;
           x[q + 3] = f.w;
+        }
+        if (homog) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) x[q] = (sc + c0 + q == v) ? 1.f : 0.f;
         }
         tc::tmem_st16(tc::tmem_addr(tmem, lane_base, kTmS + sc + c0), x);
       }
@@ -560,12 +593,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int u = 0; u < 16; ++u) vv[u] = __bfloat162float(vt[(t0c + u) * kHeadDim + v]);
         const float* bet = sm.gate(s, GA_BETA) + t0c;
+        const float vmul = homog ? 0.f : 1.f;  // a state map's homogeneous part: v taken as 0
         const float* bg = sm.gate(s, GA_BG) + t0c;
         tc::tmem_wait_ld();
         uint32_t hi[8], lo[8];
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
-          const float4 b4 = *reinterpret_cast<const float4*>(bet + 4 * u4);
+          float4 b4 = *reinterpret_cast<const float4*>(bet + 4 * u4);
+          b4.x *= vmul;
+          b4.y *= vmul;
+          b4.z *= vmul;
+          b4.w *= vmul;
           const float4 g4 = *reinterpret_cast<const float4*>(bg + 4 * u4);
           const float r0 = fmaf(b4.x, vv[4 * u4 + 0], -g4.x * x[4 * u4 + 0]);
           const float r1 = fmaf(b4.y, vv[4 * u4 + 1], -g4.y * x[4 * u4 + 1]);
@@ -627,9 +665,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (nchunks > 0)
       ok = group_wait(sm, B_MMA4 + ((nchunks - 1) & 1), ((nchunks - 1) >> 1) & 1, 1, kChainThreads, leader) &&
            !*sm.abort_flag();
-    if (ok) {
+    float* fin_blk = final_block();
+    if (ok && fin_blk) {
       tc::fence_after_sync();
-      float* dst = p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh + (size_t)v * kHeadDim + sc;
+      float* dst = fin_blk + (size_t)v * kHeadDim + sc;
 #pragma unroll 1
       for (int c8 = 0; c8 < kStateCols / 8; ++c8) {
         float x[8];
@@ -681,11 +720,105 @@ bool make_map(CUtensorMap* m, const void* base, int64_t tokens, int heads, int64
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Composition of the segment state maps (context parallelism inside the GPU):
+// S_in(s + 1) = S_in(s) M_s + C_s for s = 1 .. S - 2, fp32 on the CUDA cores.  The
+// state rows are independent under the maps, so a CTA carries its 32 rows of one
+// (sequence, v-head) through every step without synchronising with other CTAs.
+__global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
+  __shared__ __align__(16) float rows[32][kHeadDim];
+  const int h = blockIdx.x, n = blockIdx.y, r0 = blockIdx.z * 32;
+  const int tid = threadIdx.x, c = tid & 127, rh = (tid >> 7) * 16;  // column; first of 16 rows
+  const int S = p.cp_segments;
+  const float* in1 = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, 0, h) + (int64_t)r0 * kHeadDim;
+  for (int e = tid; e < 32 * kHeadDim / 4; e += 256)
+    reinterpret_cast<float4*>(&rows[0][0])[e] = reinterpret_cast<const float4*>(in1)[e];
+  __syncthreads();
+  for (int sg = 1; sg <= S - 2; ++sg) {
+    const float* M = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpMap, n, sg - 1, h);
+    const float* C = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpOff, n, sg - 1, h) + (int64_t)r0 * kHeadDim;
+    float acc[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = C[(rh + r) * kHeadDim + c];
+#pragma unroll 2
+    for (int k = 0; k < kHeadDim; k += 4) {
+      const float m0 = M[(k + 0) * kHeadDim + c], m1 = M[(k + 1) * kHeadDim + c];
+      const float m2 = M[(k + 2) * kHeadDim + c], m3 = M[(k + 3) * kHeadDim + c];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const float4 x = *reinterpret_cast<const float4*>(&rows[rh + r][k]);
+        acc[r] = fmaf(x.x, m0, acc[r]);
+        acc[r] = fmaf(x.y, m1, acc[r]);
+        acc[r] = fmaf(x.z, m2, acc[r]);
+        acc[r] = fmaf(x.w, m3, acc[r]);
+      }
+    }
+    __syncthreads();  // every thread has read the rows of S_in(sg)
+    float* out = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, sg, h) + (int64_t)r0 * kHeadDim;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      rows[rh + r][c] = acc[r];
+      out[(rh + r) * kHeadDim + c] = acc[r];
+    }
+    __syncthreads();
+  }
+}
+
+int device_sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
 }  // namespace
 
-size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads) {
+cudaError_t launch_prefill_combine(const PrefillParams& p, cudaStream_t stream) {
+  if (p.cp_segments < 3) return cudaSuccess;
+  prefill_combine_kernel<<<dim3(p.HV, p.N, kHeadDim / 32), 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  const int req = (int)((flags >> kPrefillSegmentsShift) & 15u);
+  if (req >= 1) return req;
+  // automatic, for sequences of 16 chunks or more on average.  With c (sequence, v-head)
+  // chains and m SMs, one chain per sequence takes waves(c) = ceil(c / m) chain-lengths;
+  // S segments take waves(c (2 S - 3)) + waves(c (S - 1)) segment-lengths of 1/S (pass 1
+  // and the reruns).  The cheapest S in [3, 8] is used if it saves at least 10 %.
+  const int64_t chains = (int64_t)num_seqs * num_v_heads;
+  if (chains <= 0 || total_tokens < (int64_t)num_seqs * 16 * kC) return 1;
+  const int64_t sms = device_sm_count();
+  auto waves = [&](int64_t ctas) { return (double)((ctas + sms - 1) / sms); };
+  const double one = waves(chains);
+  double best = one;
+  int best_s = 1;
+  for (int sg = 3; sg <= 8; ++sg) {
+    const double cost = (waves(chains * (2 * sg - 3)) + waves(chains * (sg - 1))) / sg;
+    if (cost < best) {
+      best = cost;
+      best_s = sg;
+    }
+  }
+  return best <= 0.9 * one ? best_s : 1;
+}
+
+size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
   if (num_seqs <= 0 || total_tokens <= 0 || num_v_heads <= 0) return 0;
-  return (size_t)chunk::num_slots(total_tokens, num_seqs) * (size_t)num_v_heads * chunk::kRecBytes;
+  const size_t records = (size_t)chunk::num_slots(total_tokens, num_seqs) * (size_t)num_v_heads * chunk::kRecBytes;
+  const int S = prefill_cp_segments(num_seqs, total_tokens, num_v_heads, flags);
+  if (S <= 1) return records;
+  return ((records + 255) & ~(size_t)255) + (size_t)cp_floats(num_seqs, num_v_heads, S) * sizeof(float);
 }
 
 bool prefill_chunk_supported(const PrefillParams& p) {
@@ -696,7 +829,7 @@ bool prefill_chunk_supported(const PrefillParams& p) {
   if (p.T <= 0) return false;
   // the prep kernel's records
   if (!p.workspace || (reinterpret_cast<uintptr_t>(p.workspace) & 15) ||
-      p.workspace_bytes < prefill_chunk_workspace_bytes(p.N, p.T, p.HV))
+      p.workspace_bytes < prefill_chunk_workspace_bytes(p.N, p.T, p.HV, p.flags))
     return false;
   // output rows leave through 256-byte bulk stores
   if ((reinterpret_cast<uintptr_t>(p.out) & 15) || (p.o_st & 7) || (p.o_sh & 7)) return false;
@@ -723,7 +856,27 @@ cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  prefill_chunk_kernel<<<dim3(p.HV, p.N), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, p);
+  const int S = prefill_cp_segments(p.N, p.T, p.HV, p.flags);
+  if (S <= 1) {
+    PrefillParams q = p;
+    q.cp_segments = 1;
+    q.cp_pass = 0;
+    prefill_chunk_kernel<<<dim3(p.HV, p.N), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+    return cudaGetLastError();
+  }
+  // context parallelism: segment maps, their composition, the segment reruns
+  const size_t records = (size_t)chunk::num_slots(p.T, p.N) * (size_t)p.HV * chunk::kRecBytes;
+  PrefillParams q = p;
+  q.cp_segments = S;
+  q.cp_scratch = reinterpret_cast<float*>(static_cast<unsigned char*>(p.workspace) + ((records + 255) & ~(size_t)255));
+  q.cp_pass = 1;
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, S >= 3 ? 2 * S - 3 : 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = launch_prefill_combine(q, stream);
+  if (e != cudaSuccess) return e;
+  q.cp_pass = 3;
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, S - 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
   return cudaGetLastError();
 }
 

@@ -50,6 +50,23 @@ __host__ __device__ inline int64_t num_slots(int64_t total_tokens, int num_seqs)
   return total_tokens / kC + num_seqs + 1;
 }
 
+// Context-parallel scratch: three arrays of [N][count][HV][128 x 128] fp32 states
+//   kCpIn  count S - 1: the initial state of segment idx + 1
+//   kCpMap count S - 2: M of segment idx + 1 (its state map is S_out = S_in M + C)
+//   kCpOff count S - 2: C of segment idx + 1
+enum CpArray { kCpIn = 0, kCpMap = 1, kCpOff = 2 };
+constexpr int64_t kStateFloats = 128 * 128;
+__host__ __device__ inline int64_t cp_floats(int N, int HV, int S) {
+  return S < 3 ? (S == 2 ? (int64_t)N * HV * kStateFloats : 0) : (int64_t)N * HV * kStateFloats * (3 * S - 5);
+}
+__host__ __device__ inline int64_t cp_offset(int N, int HV, int S, int which, int n, int idx, int h) {
+  const int64_t in_n = (int64_t)N * (S - 1) * HV * kStateFloats;
+  const int64_t map_n = S >= 3 ? (int64_t)N * (S - 2) * HV * kStateFloats : 0;
+  const int count = which == kCpIn ? S - 1 : S - 2;
+  const int64_t base = which == kCpIn ? 0 : (which == kCpMap ? in_n : in_n + map_n);
+  return base + (((int64_t)n * count + idx) * HV + h) * kStateFloats;
+}
+
 __device__ __forceinline__ int64_t load_cu(const PrefillParams& p, int i) {
   return p.cu_is_int64 ? reinterpret_cast<const int64_t*>(p.cu_seqlens)[i]
                        : (int64_t) reinterpret_cast<const int32_t*>(p.cu_seqlens)[i];
@@ -92,6 +109,7 @@ __device__ __forceinline__ void token_gates(float eA, float dt_bias, float a, fl
 
 // Launches the prep kernel over every chunk slot and v-head (mapK: the chain
 // kernel's K tensor map, 64-token x 64-feature SW128 boxes).
+cudaError_t launch_prefill_combine(const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_prefill_prep(const PrefillParams& p, const CUtensorMap& mapK, cudaStream_t stream);
 
 }  // namespace gdn

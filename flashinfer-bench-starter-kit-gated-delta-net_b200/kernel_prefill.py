@@ -45,8 +45,8 @@ _workspaces: dict = {}
 
 
 def workspace_size(num_seqs: int, total_tokens: int, num_qk_heads: int, num_v_heads: int,
-                   head_dim: int = 128, use_qk_l2norm: bool = False) -> int:
-    flags = _lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0
+                   head_dim: int = 128, use_qk_l2norm: bool = False, segments: int = 0) -> int:
+    flags = (_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0) | _lib.GDN_PREFILL_SEGMENTS(segments)
     return int(_lib.library().gdn_prefill_workspace_size(num_seqs, total_tokens, num_qk_heads,
                                                          num_v_heads, head_dim, flags))
 
@@ -63,7 +63,8 @@ def _workspace(device, nbytes: int):
 
 
 def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
-            use_qk_l2norm: bool = False, serial: bool = False, workspace=None, no_alloc: bool = False):
+            use_qk_l2norm: bool = False, serial: bool = False, workspace=None, no_alloc: bool = False,
+            segments: int = 0):
     """Destination-passing prefill: writes ``output`` [T,HV,128] bf16 and
     ``new_state`` [N,HV,128,128] fp32 (which may be ``state`` itself).
 
@@ -71,7 +72,11 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     16-byte aligned and ``use_qk_l2norm`` is off; otherwise (or with
     ``serial=True``, a cross-checking switch) the token-serial CUDA kernel runs.
     ``no_alloc=True`` calls ``gdn_prefill_noalloc`` (the library's static scratch
-    instead of a workspace buffer; problems larger than it are rejected)."""
+    instead of a workspace buffer; problems larger than it are rejected).
+    ``segments`` splits each sequence's chunks into that many ranges run on
+    separate SMs (context parallelism; 0 = the library decides, 1 = never)."""
+    if not 0 <= int(segments) <= 15:
+        raise ValueError(f"segments must be in [0, 15], got {segments}")
     T, HQ, D = q.shape
     HV = v.shape[1]
     N = cu_seqlens.shape[0] - 1
@@ -88,6 +93,7 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     if state is not None and not state.is_contiguous() and state is not new_state:
         state = state.contiguous()
     flags = (_lib.GDN_FLAG_QK_L2NORM if use_qk_l2norm else 0) | (_lib.GDN_FLAG_PREFILL_SERIAL if serial else 0)
+    flags |= _lib.GDN_PREFILL_SEGMENTS(segments)
     lib = _lib.library()
     if no_alloc:
         rc = lib.gdn_prefill_noalloc(ptr(q), *seq_head_strides(q, 0, 1), ptr(k), *seq_head_strides(k, 0, 1),
@@ -119,7 +125,7 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
 
 
 def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2norm: bool = False,
-        serial: bool = False):
+        serial: bool = False, segments: int = 0):
     """Value-returning prefill (the reference's ``run``): returns
     ``(output [T,HV,128] bf16, new_state [N,HV,128,128] fp32)``."""
     T, _, D = q.shape
@@ -128,4 +134,4 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
     output = torch.empty(T, HV, D, dtype=torch.bfloat16, device=q.device)
     new_state = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
     return run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
-                   use_qk_l2norm=use_qk_l2norm, serial=serial)
+                   use_qk_l2norm=use_qk_l2norm, serial=serial, segments=segments)

@@ -48,6 +48,11 @@ extern "C" {
 #define GDN_FLAG_QK_L2NORM 0x1u      /* L2-normalise q and k inside the kernel (eps 1e-6); default off */
 #define GDN_FLAG_PREFILL_SERIAL 0x2u /* prefill: use the token-serial kernel instead of the chunked
                                         tensor-core kernel (cross-checking; prefill only) */
+/* Prefill: split each sequence's chunks into n segments (2..15) that run on separate SMs
+ * (context parallelism: per-segment affine state maps, composed, then the segments rerun
+ * from their initial states).  0 = automatic (segments only when the (sequence, v-head)
+ * chains leave most SMs idle and sequences are long), 1 = never.  Bits 8-11. */
+#define GDN_PREFILL_SEGMENTS(n) ((((uint32_t)(n)) & 15u) << 8)
 
 /* Device-side error bits reported by gdn_device_error(). */
 #define GDN_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded wait inside a kernel gave up */

@@ -104,6 +104,22 @@ def test_workspace_size(lib):
     assert lib.gdn_prefill_workspace_size(0, 0, 16, 32, 128, 0) == 0
 
 
+def test_workspace_size_with_segments(lib):
+    """Context-parallel segments add [N][3 S - 5][HV] 64 KB states (segment starts,
+    maps M and C) after the records, 256-byte aligned.  Automatic: one long sequence
+    with 32 v-heads (32 chains on 148 SMs) gets S = 5 (pass 1: 224 CTAs in 2 waves,
+    reruns: 128 in 1 wave, 3/5 of one chain's length); many or short sequences get none."""
+    seg = lambda n: (n & 15) << 8  # noqa: E731  (GDN_PREFILL_SEGMENTS)
+    rec = lambda n, t: (t // 64 + n + 1) * 32 * 17664  # noqa: E731
+    st = 128 * 128 * 4
+    assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(3)) == rec(2, 3000) + 2 * 32 * st * 4
+    assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(2)) == rec(2, 3000) + 2 * 32 * st * 1
+    assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(1)) == rec(2, 3000)
+    assert lib.gdn_prefill_workspace_size(1, 4096, 16, 32, 128, 0) == rec(1, 4096) + 32 * st * 10
+    assert lib.gdn_prefill_workspace_size(1, 512, 16, 32, 128, 0) == rec(1, 512)  # < 16 chunks
+    assert lib.gdn_prefill_workspace_size(2, 8192, 16, 32, 128, 0) == rec(2, 8192)  # 64 chains
+
+
 def test_missing_library_fails_loudly(gdn, monkeypatch, tmp_path):
     monkeypatch.setattr(gdn._lib, "_lib", None)
     monkeypatch.setenv("GDN_B200_LIB", str(tmp_path / "nope.so"))
