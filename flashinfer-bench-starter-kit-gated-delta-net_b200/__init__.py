@@ -5,13 +5,17 @@ Drop-in for the two entry points of the reference solution
 the same tensors, dtypes, k-last fp32 state layout and value-returning
 ``(output, new_state)`` contract, computed by hand-written sm_100a CUDA
 kernels in ``libgdn_b200.so`` reached through a C ABI (``include/gdn_b200.h``).
-``kernel_mtp`` adds the serving form: multi-token decode against a state pool.
+``kernel_mtp`` adds the serving form: multi-token decode against a state pool;
+``context_parallel`` spreads one prefill of few long sequences over the ranks of a
+process group (affine state maps exchanged once).
 There is no CPU or Triton fallback: without the built library on a CUDA
 device every operator raises.
 """
 from . import workloads  # noqa: F401  (CPU-only helpers, always importable)
 from . import sharding  # noqa: F401
 from . import kernel_decode, kernel_prefill, kernel_mtp  # noqa: F401
+from . import context_parallel  # noqa: F401
 from ._lib import library, library_path  # noqa: F401
 
-__all__ = ["kernel_decode", "kernel_prefill", "kernel_mtp", "workloads", "sharding", "library", "library_path"]
+__all__ = ["kernel_decode", "kernel_prefill", "kernel_mtp", "context_parallel", "workloads", "sharding", "library",
+           "library_path"]

@@ -70,6 +70,12 @@ SIGNATURES = {
                              _P, _I64, _I64, _P, _I64, _I64,                   # out, new_state
                              _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
                              _U32, _P], ctypes.c_int),
+    "gdn_prefill_state_map": ([_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,  # q, k, v
+                               _P, _P, _I64, _P, _P, _I64,                       # A_log, a, dt_bias, b
+                               _P, _I32,                                         # cu_seqlens
+                               _P, _I64, _I64, _P, _I64, _I64,                   # map_m, map_c
+                               _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
+                               _P, _SZ, _U32, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -11,12 +11,13 @@ DTYPES = {"q": _BF16, "k": _BF16, "v": _BF16, "a": _BF16, "b": _BF16, "output": 
           "A_log": _F32, "dt_bias": _F32, "state": _F32, "new_state": _F32}
 
 
-def check_cuda(q, k, v, A_log, a, dt_bias, b, output, new_state, state=None):
-    """All tensors on one CUDA device with the definition's dtypes."""
-    named = dict(q=q, k=k, v=v, A_log=A_log, a=a, dt_bias=dt_bias, b=b, output=output,
-                 new_state=new_state)
-    if state is not None:
-        named["state"] = state
+def check_cuda(q, k, v, A_log, a, dt_bias, b, output=None, new_state=None, state=None):
+    """All tensors on one CUDA device with the definition's dtypes (output, new_state
+    and state are checked when given)."""
+    named = dict(q=q, k=k, v=v, A_log=A_log, a=a, dt_bias=dt_bias, b=b)
+    for name, t in (("output", output), ("new_state", new_state), ("state", state)):
+        if t is not None:
+            named[name] = t
     dev = q.device
     if dev.type != "cuda":
         raise RuntimeError("gdn_b200 operators run on CUDA tensors only (no CPU implementation)")

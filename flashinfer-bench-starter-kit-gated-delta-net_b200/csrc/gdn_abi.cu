@@ -342,6 +342,82 @@ int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h, const voi
   return ok();
 }
 
+int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+                          int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_t,
+                          int64_t v_stride_h, const float* A_log, const void* a, int64_t a_stride_t,
+                          const float* dt_bias, const void* b, int64_t b_stride_t, const void* cu_seqlens,
+                          int32_t cu_seqlens_is_int64, float* map_m, int64_t map_m_stride_n, int64_t map_m_stride_h,
+                          float* map_c, int64_t map_c_stride_n, int64_t map_c_stride_h, int32_t num_seqs,
+                          int64_t total_tokens, int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                          void* workspace, size_t workspace_bytes, uint32_t flags, void* stream) {
+  int rc = check_common(num_qk_heads, num_v_heads, head_dim);
+  if (rc) return rc;
+  if (num_seqs < 0 || total_tokens < 0)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0 (got %d, %lld)", num_seqs,
+                (long long)total_tokens);
+  if (num_seqs > 65535) return fail(GDN_ERR_UNSUPPORTED, "num_seqs > 65535 per call is not supported");
+  if (flags) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_prefill_state_map takes no flags (got 0x%x)", flags);
+  if (num_seqs == 0) return ok();
+  if (!cu_seqlens || !A_log || !dt_bias || !map_m || !map_c)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (!aligned(map_m, map_m_stride_n, map_m_stride_h, sizeof(float), 16) ||
+      !aligned(map_c, map_c_stride_n, map_c_stride_h, sizeof(float), 16))
+    return fail(GDN_ERR_UNSUPPORTED, "map rows must be 16-byte aligned (base and strides)");
+  if (total_tokens > 0) {
+    if (!q || !k || !v || !a || !b) return fail(GDN_ERR_INVALID_ARGUMENT, "a required tensor pointer is NULL");
+    if (!aligned(q, q_stride_t, q_stride_h, 2, 16) || !aligned(k, k_stride_t, k_stride_h, 2, 16) ||
+        !aligned(v, v_stride_t, v_stride_h, 2, 16))
+      return fail(GDN_ERR_UNSUPPORTED, "gdn_prefill_state_map needs 16-byte aligned q/k/v rows (base and strides)");
+  }
+  const size_t need = gdn::prefill_chunk_workspace_bytes(num_seqs, total_tokens, num_v_heads, GDN_PREFILL_SEGMENTS(1));
+  if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15)))
+    return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required (got %zu)", need,
+                workspace_bytes);
+  gdn::PrefillParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.state = nullptr;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.cu_seqlens = cu_seqlens;
+  p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
+  p.out = nullptr;
+  p.new_state = nullptr;
+  p.q_st = q_stride_t;
+  p.q_sh = q_stride_h;
+  p.k_st = k_stride_t;
+  p.k_sh = k_stride_h;
+  p.v_st = v_stride_t;
+  p.v_sh = v_stride_h;
+  p.s_sn = p.s_sh = 0;
+  p.a_st = a_stride_t;
+  p.b_st = b_stride_t;
+  p.o_st = p.o_sh = 0;
+  p.n_sn = p.n_sh = 0;
+  p.scale = 1.0f;
+  p.N = num_seqs;
+  p.HQ = num_qk_heads;
+  p.HV = num_v_heads;
+  p.ratio = num_v_heads / num_qk_heads;
+  p.T = total_tokens;
+  p.flags = GDN_PREFILL_SEGMENTS(1);
+  p.workspace = workspace;
+  p.workspace_bytes = workspace_bytes;
+  p.map_m = map_m;
+  p.m_sn = map_m_stride_n;
+  p.m_sh = map_m_stride_h;
+  p.map_c = map_c;
+  p.c_sn = map_c_stride_n;
+  p.c_sh = map_c_stride_h;
+  const cudaError_t e = total_tokens > 0 ? gdn::launch_prefill_state_map(p, static_cast<cudaStream_t>(stream))
+                                         : gdn::launch_identity_maps(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill_state_map launch");
+  return ok();
+}
+
 int gdn_prefill_noalloc(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k, int64_t k_stride_t,
                         int64_t k_stride_h, const void* v, int64_t v_stride_t, int64_t v_stride_h,
                         const float* state, int64_t state_stride_n, int64_t state_stride_h, const float* A_log,

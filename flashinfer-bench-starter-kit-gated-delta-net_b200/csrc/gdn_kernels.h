@@ -62,6 +62,10 @@ struct PrefillParams {
   int cp_segments = 1;
   int cp_pass = 0;
   float* cp_scratch = nullptr;
+  // cp_pass 2: each sequence's affine state map S_out = S_in M + C instead of a prefill
+  float* map_m = nullptr;
+  float* map_c = nullptr;
+  int64_t m_sn = 0, m_sh = 0, c_sn = 0, c_sh = 0;
 };
 
 // Multi-token decode against a state pool (serving form).  Strides in elements;
@@ -110,5 +114,10 @@ constexpr int kPrefillSegmentsShift = 8;
 int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
 bool prefill_chunk_supported(const PrefillParams& p);
 cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream);
+// Per sequence the affine map of its token range, M [HV][K][K] and C [HV][V][K]
+// (S_out = S_in M + C): the chunked chain from the identity with v = 0 and from zero.
+cudaError_t launch_prefill_state_map(const PrefillParams& p, cudaStream_t stream);
+// The maps of empty token ranges: M = I, C = 0 for every sequence and v-head.
+cudaError_t launch_identity_maps(const PrefillParams& p, cudaStream_t stream);
 
 }  // namespace gdn

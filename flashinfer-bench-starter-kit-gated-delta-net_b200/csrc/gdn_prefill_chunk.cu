@@ -200,15 +200,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   //   2 s - 1 = M of segment s (identity start, v taken as 0), 2 s = C of segment s
   //   (zero start), no outputs (s = 1 .. S - 2).
   // cp_pass 3 (z): segment z + 1 from kCpIn[z], with outputs; the last one ends in p.new_state.
+  // cp_pass 2 (z): the whole sequence's map, 0 = M -> p.map_m, 1 = C -> p.map_c, no outputs.
   const int S = p.cp_segments, cz = blockIdx.z;
   const int seg = p.cp_pass == 1 ? (cz + 1) >> 1 : (p.cp_pass == 3 ? cz + 1 : 0);
-  const bool emit = p.cp_pass != 1 || cz == 0;          // outputs of the range are written
-  const bool homog = p.cp_pass == 1 && (cz & 1);        // identity start, v taken as 0 (an M)
+  const bool emit = p.cp_pass == 0 || p.cp_pass == 3 || (p.cp_pass == 1 && cz == 0);  // outputs written
+  const bool homog = (p.cp_pass == 1 && (cz & 1)) || (p.cp_pass == 2 && cz == 0);     // identity start, v = 0
   // where the range's state starts (nullptr: zero, or the identity when homog) and ends
   // (nullptr: not stored); evaluated where used, to keep them out of the loops' registers
   auto init_block = [&]() -> const float* {
     if (p.cp_pass == 3) return p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, seg - 1, h);
-    if (p.cp_pass == 1 && cz != 0) return nullptr;
+    if ((p.cp_pass == 1 && cz != 0) || p.cp_pass == 2) return nullptr;
     return p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh : nullptr;
   };
   auto final_block = [&]() -> float* {
@@ -216,6 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       return p.cp_scratch + (cz == 0 ? cp_offset(p.N, p.HV, S, kCpIn, n, 0, h)
                                      : cp_offset(p.N, p.HV, S, (cz & 1) ? kCpMap : kCpOff, n, seg - 1, h));
     if (p.cp_pass == 3 && seg != S - 1) return nullptr;
+    if (p.cp_pass == 2)
+      return cz == 0 ? p.map_m + (size_t)n * p.m_sn + (size_t)h * p.m_sh : p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh;
     return p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh;
   };
   const int nch_seq = (int)((seq_len + kC - 1) / kC);
@@ -836,15 +839,19 @@ bool prefill_chunk_supported(const PrefillParams& p) {
   return ok16(p.q, p.q_st, p.q_sh) && ok16(p.k, p.k_st, p.k_sh) && ok16(p.v, p.v_st, p.v_sh);
 }
 
-cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream) {
-  if (p.N == 0) return cudaSuccess;
-  CUtensorMap mk, mq, mv, mo;
-  if (!make_map(&mk, p.k, p.T, p.HQ, p.k_st, p.k_sh, 64, true) ||
-      !make_map(&mq, p.q, p.T, p.HQ, p.q_st, p.q_sh, 64, true) ||
-      !make_map(&mv, p.v, p.T, p.HV, p.v_st, p.v_sh, 128, false) ||
-      !make_map(&mo, p.out, p.T, p.HV, p.o_st, p.o_sh, 128, false))
+namespace {
+// Tensor maps of one call, the prep launch and the chain kernel's shared-memory opt-in.
+// A state-map call has no output tensor: its output map is built on q (never stored to).
+cudaError_t prefill_setup(const PrefillParams& p, cudaStream_t stream, CUtensorMap* mk, CUtensorMap* mq,
+                          CUtensorMap* mv, CUtensorMap* mo) {
+  const bool map_only = p.cp_pass == 2;
+  if (!make_map(mk, p.k, p.T, p.HQ, p.k_st, p.k_sh, 64, true) ||
+      !make_map(mq, p.q, p.T, p.HQ, p.q_st, p.q_sh, 64, true) ||
+      !make_map(mv, p.v, p.T, p.HV, p.v_st, p.v_sh, 128, false) ||
+      !make_map(mo, map_only ? const_cast<__nv_bfloat16*>(p.q) : p.out, p.T, map_only ? p.HQ : p.HV,
+                map_only ? p.q_st : p.o_st, map_only ? p.q_sh : p.o_sh, 128, false))
     return cudaErrorInvalidValue;
-  cudaError_t e = launch_prefill_prep(p, mk, stream);
+  cudaError_t e = launch_prefill_prep(p, *mk, stream);
   if (e != cudaSuccess) return e;
   // The dynamic shared-memory opt-in is a per-device function attribute.
   static bool attr_set[64] = {};
@@ -856,6 +863,45 @@ cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
+  return cudaSuccess;
+}
+
+__global__ void identity_maps_kernel(PrefillParams p) {
+  const int h = blockIdx.x, n = blockIdx.y;
+  float* m = p.map_m + (size_t)n * p.m_sn + (size_t)h * p.m_sh;
+  float* c = p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh;
+  for (int e = threadIdx.x; e < kHeadDim * kHeadDim; e += blockDim.x) {
+    m[e] = (e / kHeadDim == e % kHeadDim) ? 1.f : 0.f;
+    c[e] = 0.f;
+  }
+}
+}  // namespace
+
+cudaError_t launch_identity_maps(const PrefillParams& p, cudaStream_t stream) {
+  if (p.N == 0) return cudaSuccess;
+  identity_maps_kernel<<<dim3(p.HV, p.N), 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_state_map(const PrefillParams& p, cudaStream_t stream) {
+  if (p.N == 0) return cudaSuccess;
+  PrefillParams q = p;
+  q.cp_segments = 1;
+  q.cp_pass = 2;
+  q.out = nullptr;
+  q.new_state = nullptr;
+  CUtensorMap mk, mq, mv, mo;
+  cudaError_t e = prefill_setup(q, stream, &mk, &mq, &mv, &mo);
+  if (e != cudaSuccess) return e;
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream) {
+  if (p.N == 0) return cudaSuccess;
+  CUtensorMap mk, mq, mv, mo;
+  cudaError_t e = prefill_setup(p, stream, &mk, &mq, &mv, &mo);
+  if (e != cudaSuccess) return e;
   const int S = prefill_cp_segments(p.N, p.T, p.HV, p.flags);
   if (S <= 1) {
     PrefillParams q = p;

@@ -135,3 +135,41 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
     new_state = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
     return run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
                    use_qk_l2norm=use_qk_l2norm, serial=serial, segments=segments)
+
+
+def state_map(q, k, v, A_log, a, dt_bias, b, cu_seqlens, map_m=None, map_c=None, *, workspace=None):
+    """Affine state map of each sequence's token range (C ABI ``gdn_prefill_state_map``):
+    running the range from any initial state S gives ``S_out = S @ M + C`` per
+    (sequence, v-head), with ``M`` [N,HV,128,128] the range run from the identity with
+    v taken as 0 and ``C`` [N,HV,128,128] the range run from zero.  No counterpart in
+    the reference; context parallelism composes these maps across ranks."""
+    T, HQ, D = q.shape
+    HV = v.shape[1]
+    N = cu_seqlens.shape[0] - 1
+    check_cuda(q, k, v, A_log, a, dt_bias, b)
+    if cu_seqlens.device != q.device:
+        raise ValueError("cu_seqlens must be on the same device as q")
+    if cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
+    if map_m is None:
+        map_m = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
+    if map_c is None:
+        map_c = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
+    check_cuda(q, k, v, A_log, a, dt_bias, b, new_state=map_m, state=map_c)
+    q, k, v = inner_contig(q), inner_contig(k), inner_contig(v)
+    a, b = inner_contig(a), inner_contig(b)
+    A_log, dt_bias, cu = A_log.contiguous(), dt_bias.contiguous(), cu_seqlens.contiguous()
+    lib = _lib.library()
+    need = int(lib.gdn_prefill_workspace_size(N, T, HQ, HV, D, _lib.GDN_PREFILL_SEGMENTS(1)))
+    if workspace is None:
+        workspace = _workspace(q.device, need)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = lib.gdn_prefill_state_map(ptr(q), *seq_head_strides(q, 0, 1), ptr(k), *seq_head_strides(k, 0, 1),
+                                   ptr(v), *seq_head_strides(v, 0, 1),
+                                   ptr(A_log), ptr(a), a.stride(0), ptr(dt_bias), ptr(b), b.stride(0),
+                                   ptr(cu), int(cu.dtype == torch.int64),
+                                   ptr(map_m), *seq_head_strides(map_m, 0, 1),
+                                   ptr(map_c), *seq_head_strides(map_c, 0, 1),
+                                   N, T, HQ, HV, D, ptr(workspace), ws_bytes, 0, stream_handle(q.device))
+    _lib.check(rc)
+    return map_m, map_c

@@ -172,6 +172,37 @@ GDN_API int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                 void* workspace, size_t workspace_bytes,
                 uint32_t flags, void* stream);
 
+/*
+ * Affine state map of each sequence's token range (no counterpart in the reference,
+ * whose prefill is token-serial; the building block of context parallelism across
+ * GPUs, where a rank holding a later range of a sequence needs its map before the
+ * state entering the range is known).  The recurrence is affine in the state: for
+ * sequence n and v-head h, running the range from any initial state S gives
+ *   S_out = S M + C      (k-last [V x K] states, row vectors; fp32)
+ * with M [K x K] the range run from the identity with v taken as 0 and C [V x K]
+ * the range run from a zero state.  Inputs as gdn_prefill (no state, no outputs);
+ * q/k/v rows and strides 16-byte aligned.  Writes
+ *   map_m [N, num_v_heads, head_dim, head_dim]   strides (n, h), rows contiguous
+ *   map_c [N, num_v_heads, head_dim, head_dim]   strides (n, h), rows contiguous
+ * An empty range gives M = I, C = 0.  workspace: at least
+ * gdn_prefill_workspace_size(..., GDN_PREFILL_SEGMENTS(1)) bytes, 16-byte aligned.
+ * flags must be 0.
+ */
+GDN_API int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                const void* k, int64_t k_stride_t, int64_t k_stride_h,
+                const void* v, int64_t v_stride_t, int64_t v_stride_h,
+                const float* A_log,
+                const void* a, int64_t a_stride_t,
+                const float* dt_bias,
+                const void* b, int64_t b_stride_t,
+                const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                float* map_m, int64_t map_m_stride_n, int64_t map_m_stride_h,
+                float* map_c, int64_t map_c_stride_n, int64_t map_c_stride_h,
+                int32_t num_seqs, int64_t total_tokens,
+                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                void* workspace, size_t workspace_bytes,
+                uint32_t flags, void* stream);
+
 /* Bytes of device workspace gdn_prefill needs for this problem size. */
 GDN_API size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_t num_qk_heads,
                                   int32_t num_v_heads, int32_t head_dim, uint32_t flags);

@@ -87,3 +87,81 @@ def test_segments_in_place_without_allocation(gdn):
                                dev["b"], dev["cu_seqlens"], dev["scale"], out, state, no_alloc=True, segments=4)
     torch.cuda.synchronize()
     assert_match(out, state, o_ref, s_ref)
+
+
+def _oracle_map(inp):
+    N, H = inp["cu_seqlens"].shape[0] - 1, inp["v"].shape[1]
+    eye = np.broadcast_to(np.eye(128, dtype=np.float32), (N, H, 128, 128)).copy()
+    args = (inp["A_log"].cpu().numpy(), bits(inp["a"]), inp["dt_bias"].cpu().numpy(), bits(inp["b"]),
+            inp["cu_seqlens"].cpu().numpy(), None)
+    _, m = c_oracle.prefill(bits(inp["q"]), bits(inp["k"]), np.zeros_like(bits(inp["v"])), eye, *args)
+    _, c = c_oracle.prefill(bits(inp["q"]), bits(inp["k"]), bits(inp["v"]), None, *args)
+    return m, c
+
+
+@pytest.mark.parametrize("slow_decay", [False, True])
+def test_state_map_matches_oracle_and_is_affine(gdn, slow_decay):
+    """M = the range from the identity with v = 0, C = the range from zero; and the
+    prefill from any state S ends in S M + C.  With the benchmark gates the state
+    forgets its start within tens of tokens (M falls to 1e-18 .. 1e-38 on the short
+    ranges), so M is checked to 1e-3 of its size plus 1e-6 absolute (S M then errs
+    by far less than the 1e-3 state tolerance); with slow decay (A_log = -6) M stays
+    O(1) and the check is relative."""
+    lens = [0, 37, 700, 130]
+    inp = gdn.workloads.prefill_inputs(lens, seed=330)
+    if slow_decay:
+        inp["A_log"] = torch.full_like(inp["A_log"], -6.0)
+    dev = to_dev(inp)
+    M, C = gdn.kernel_prefill.state_map(dev["q"], dev["k"], dev["v"], dev["A_log"], dev["a"], dev["dt_bias"],
+                                        dev["b"], dev["cu_seqlens"])
+    torch.cuda.synchronize()
+    m_ref, c_ref = _oracle_map(inp)
+    ok, err = state_close(C[1:].cpu().numpy(), c_ref[1:], 1e-3)
+    assert ok, err
+    dm = np.abs(M.cpu().numpy() - m_ref).reshape(len(lens), 32, -1).max(-1)
+    scale = np.abs(m_ref).reshape(len(lens), 32, -1).max(-1)
+    assert (dm <= 1e-3 * scale + 1e-6).all(), float((dm / np.maximum(scale, 1e-30)).max())
+    if slow_decay:
+        assert scale[1:].min() > 1e-3  # the maps are far from zero here (1e-2 .. 1 by head)
+    assert torch.equal(M[0], torch.eye(128, device="cuda").expand_as(M[0])) and not C[0].any()  # empty range
+    _, fin = gdn.kernel_prefill.run(**dev, segments=1)
+    comp = torch.matmul(dev["state"], M) + C
+    torch.cuda.synchronize()
+    ok, err = state_close(comp.cpu().numpy(), fin.cpu().numpy(), 1e-4)
+    assert ok, err
+
+
+def test_context_parallel_steps_on_one_gpu(gdn):
+    """The three ranks of a context-parallel prefill emulated on one device with the
+    CUDA operators (maps, fold, reruns) against the oracle's whole sequences."""
+    cp = gdn.context_parallel
+    ops = cp.cuda_ops()
+    lens, world = [2000, 513, 64], 3
+    inp = gdn.workloads.prefill_inputs(lens, seed=340)
+    dev = to_dev(inp)
+    locs = [cp.local_inputs(dev, world, r) for r in range(world)]
+    keys = ("q", "k", "v")
+    gate = lambda L: (L["A_log"], L["a"], L["dt_bias"], L["b"], L["cu_seqlens"])  # noqa: E731
+    outs = [None] * world
+    outs[0], s = ops.prefill(*(locs[0][x] for x in keys), dev["state"], *gate(locs[0]), dev["scale"])
+    pairs = [(torch.zeros_like(s), s)] + [ops.state_map(*(locs[r][x] for x in keys), *gate(locs[r]))
+                                          for r in range(1, world)]
+    for r in range(1, world):
+        s_in = torch.zeros_like(s)
+        for j in range(r):
+            s_in = ops.compose(s_in, *pairs[j])
+        outs[r], s_r = ops.prefill(*(locs[r][x] for x in keys), s_in, *gate(locs[r]), dev["scale"])
+    torch.cuda.synchronize()
+    o_ref, s_ref = oracle_prefill(inp)
+    o_ref = ref.bf16_bits_to_f32(o_ref)
+    ranges = cp.split_ranges(lens, world)
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    out = np.zeros_like(o_ref)
+    for r in range(world):
+        pos, o = 0, outs[r].float().cpu().numpy()
+        for i, (lo, hi) in enumerate(ranges[r]):
+            out[cu[i] + lo:cu[i] + hi] = o[pos:pos + hi - lo]
+            pos += hi - lo
+    np.testing.assert_allclose(out, o_ref, **OUT_TOL)
+    ok, err = state_close(s_r.cpu().numpy(), s_ref, 1e-3)
+    assert ok, err
