@@ -473,7 +473,45 @@ def run_ours(args, world, rank, local):
         else:
             result["mtp"] = mres
         del msets
-    if args.prefill and not wl.startswith("prefill") and wl != "mtp_b64_t4":
+    if wl == "longctx_1x131072":
+        # one 131,072-token sequence (all 32 v-heads): 1 GPU = the prefill with its in-GPU
+        # context-parallel segments; N GPUs = context parallelism across ranks (strong scaling:
+        # the same sequence split by context_parallel.split_ranges, maps exchanged over NCCL)
+        L = 131072
+        seqlens = [L]
+        inp = gdn.workloads.prefill_inputs(seqlens, seed=11, device="cuda")
+        if world == 1:
+            inp["output"] = torch.empty(L, 32, 128, dtype=torch.bfloat16, device="cuda")
+            inp["new_state"] = torch.empty_like(inp["state"])
+            call = lambda s: prefill_call(gdn, s)  # noqa: E731
+            local_tokens, launches = L, 4  # prep, pass 1, combine, reruns
+        else:
+            loc = gdn.context_parallel.local_inputs(inp, world, rank)
+            inp = loc
+            cp = gdn.context_parallel
+
+            def call(s):
+                cp.prefill_context_parallel(s["q"], s["k"], s["v"], s["state"], s["A_log"], s["a"], s["dt_bias"],
+                                            s["b"], s["cu_seqlens"], s["scale"])
+            local_tokens = int(loc["q"].shape[0])
+            launches = 4 if rank == 0 else 7  # rank 0: prefill; others: map (prep, chains, combine) + prefill
+        sampler_l = ClockSampler(local)
+        lms, llaunch = time_steps(call, [inp], args.steps, args.warmup, world, sampler_l)
+        flops = gdn.workloads.prefill_flops_per_token() * L
+        result.update(metric="GDN long-context prefill tokens/s", value=L / (lms * 1e-3), unit="tokens/s",
+                      ms_per_step=lms, dtype="bf16",
+                      config={"workload": wl, "seqlens": seqlens, "tokens_per_rank": local_tokens,
+                              "l2": "inputs 2.3 GB, larger than L2",
+                              "parallelism": "in-GPU segments" if world == 1 else
+                              f"context parallel over {world} ranks (weighted ranges, one all_gather of state maps)"},
+                      roofline={"bound": "tensor", "achieved": flops / (lms * 1e-3) / 1e12 / world, "peak": bf16_peak,
+                                "unit": "TFLOP/s", "frac": flops / (lms * 1e-3) / 1e12 / world / bf16_peak,
+                                "peak_kind": f"{peak_kind} bf16_tflops (burst)",
+                                "note": "whole step per GPU (all kernels and collectives), algorithmic FLOPs"},
+                      gpu_launches=launches * args.steps, clocks=sampler_l.summary(), e2e=None)
+        result["scaling"] = "strong"
+        del inp
+    if args.prefill and not wl.startswith("prefill") and wl not in ("mtp_b64_t4", "longctx_1x131072"):
         wl_p = "prefill_varlen16"
     elif wl.startswith("prefill"):
         wl_p = wl
@@ -528,7 +566,8 @@ def run_ours(args, world, rank, local):
                                           "sample": sample}
         line = {"metric": result["metric"], "value": result["value"], "unit": result["unit"],
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": result["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "ms_per_step": result["ms_per_step"], "higher_is_better": True,
+                "scaling": result.pop("scaling", "weak"),
                 "vs_baseline": None, "dtype": result["dtype"], "data": "synthetic (seeded, BASELINE distributions)",
                 **{k: v for k, v in result.items() if k not in ("metric", "value", "unit", "ms_per_step", "dtype")}}
         print(json.dumps(line), flush=True)
@@ -541,7 +580,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="decode_b64",
-                    choices=["decode_b64", "decode_b1024", "prefill_varlen16", "prefill_8x32768", "mtp_b64_t4"])
+                    choices=["decode_b64", "decode_b1024", "prefill_varlen16", "prefill_8x32768", "mtp_b64_t4",
+                             "longctx_1x131072"])
     ap.add_argument("--no-prefill", dest="prefill", action="store_false",
                     help="skip the secondary configs[3] prefill measurement")
     args = ap.parse_args()

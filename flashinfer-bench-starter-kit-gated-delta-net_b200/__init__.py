@@ -7,7 +7,8 @@ the same tensors, dtypes, k-last fp32 state layout and value-returning
 kernels in ``libgdn_b200.so`` reached through a C ABI (``include/gdn_b200.h``).
 ``kernel_mtp`` adds the serving form: multi-token decode against a state pool;
 ``context_parallel`` spreads one prefill of few long sequences over the ranks of a
-process group (affine state maps exchanged once).
+process group (affine state maps exchanged once); ``harness`` runs flashinfer-bench
+workload records (definition + safetensors blobs) through the drop-in ``run``s.
 There is no CPU or Triton fallback: without the built library on a CUDA
 device every operator raises.
 """
@@ -15,7 +16,8 @@ from . import workloads  # noqa: F401  (CPU-only helpers, always importable)
 from . import sharding  # noqa: F401
 from . import kernel_decode, kernel_prefill, kernel_mtp  # noqa: F401
 from . import context_parallel  # noqa: F401
+from . import harness  # noqa: F401
 from ._lib import library, library_path  # noqa: F401
 
-__all__ = ["kernel_decode", "kernel_prefill", "kernel_mtp", "context_parallel", "workloads", "sharding", "library",
-           "library_path"]
+__all__ = ["kernel_decode", "kernel_prefill", "kernel_mtp", "context_parallel", "harness", "workloads", "sharding",
+           "library", "library_path"]

@@ -16,14 +16,18 @@ from the identity with v taken as 0 and C [V x K] the range run from zero
 4. the last rank's final state is broadcast, so every rank returns the sequences'
    final state.
 
-Each rank's work is two range-lengths of the chain (map, rerun) instead of the
-whole sequence: for R ranks, about R / 2 times the single-GPU speed on one sequence,
-on top of the in-GPU segment split ``kernel_prefill`` applies to each range.  The
+Each rank but rank 0 works two range-lengths (the map, itself computed in segments
+on separate SMs, then the rerun), rank 0 one; both use the in-GPU segment split of
+``kernel_prefill`` for few long sequences.  The
 reference has no long-context parallelism (its prefill is token-serial per
 sequence, ``solution/triton/kernel_prefill.py:88``).
 
 ``split_ranges``/``local_inputs`` cut a global varlen batch into rank-local inputs:
-every range of a sequence starts on a 64-token chunk boundary.
+every range of a sequence starts on a 64-token chunk boundary.  Rank 0 does one pass
+over its range and every other rank two (map, rerun), so rank 0's range is weighted
+``FIRST_RANK_WEIGHT`` times the others' by default: with the in-GPU segments of one
+long 32-head sequence a prefill costs ~0.6 and a map ~0.5 of one chain per token, so
+(0.5 + 0.6) / 0.6 ≈ 1.8.
 """
 from __future__ import annotations
 
@@ -34,31 +38,37 @@ import torch
 import torch.distributed as dist
 
 CHUNK = 64
+FIRST_RANK_WEIGHT = 1.8
 
 
-def split_ranges(seqlens, world: int) -> list[list[tuple[int, int]]]:
+def split_ranges(seqlens, world: int, first_weight: float = FIRST_RANK_WEIGHT) -> list[list[tuple[int, int]]]:
     """Per rank, per sequence, the token range ``[lo, hi)`` (sequence-relative) it
-    holds: a sequence's chunks are split into ``world`` contiguous runs whose sizes
-    differ by at most one chunk; the last run also takes the final partial chunk."""
+    holds: a sequence's chunks are split into ``world`` contiguous runs in proportion
+    ``first_weight : 1 : .. : 1`` (rounded down to whole chunks); the last run also
+    takes the final partial chunk."""
     if world < 1:
         raise ValueError("world must be >= 1")
+    if first_weight <= 0:
+        raise ValueError("first_weight must be > 0")
+    total = first_weight + (world - 1)
+    cum = [0.0] + [(first_weight + r - 1) / total for r in range(1, world)]
     out = [[] for _ in range(world)]
     for L in seqlens:
         L = int(L)
         nch = (L + CHUNK - 1) // CHUNK
-        bounds = [min(L, (r * nch // world) * CHUNK) for r in range(world)] + [L]
+        bounds = [min(L, int(cum[r] * nch + 1e-9) * CHUNK) for r in range(world)] + [L]
         for r in range(world):
             out[r].append((bounds[r], bounds[r + 1]))
     return out
 
 
-def local_inputs(inp: dict, world: int, rank: int) -> dict:
+def local_inputs(inp: dict, world: int, rank: int, first_weight: float = FIRST_RANK_WEIGHT) -> dict:
     """Rank ``rank``'s slice of a global prefill input dict (keys of ``kernel_prefill.run``):
     its token ranges of every sequence, concatenated, with rank-local ``cu_seqlens``.
     ``state`` is kept on every rank (only rank 0 reads it)."""
     cu = inp["cu_seqlens"].cpu().tolist()
     lens = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
-    ranges = split_ranges(lens, world)[rank]
+    ranges = split_ranges(lens, world, first_weight)[rank]
     parts = [torch.arange(cu[i] + lo, cu[i] + hi, dtype=torch.long) for i, (lo, hi) in enumerate(ranges)]
     idx = torch.cat(parts) if parts else torch.zeros(0, dtype=torch.long)
     local_cu = [0]

@@ -176,6 +176,8 @@ size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_
                                   int32_t head_dim, uint32_t flags) {
   (void)num_qk_heads;
   (void)head_dim;
+  // gdn_prefill_state_map: records + the per-segment maps
+  if (flags & GDN_FLAG_STATE_MAP) return gdn::prefill_map_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
   // the token-serial kernel (forced, or for in-kernel q/k normalisation) needs none;
   // the chunked kernel keeps one prepared record per chunk slot and v-head
   if (flags & (GDN_FLAG_PREFILL_SERIAL | GDN_FLAG_QK_L2NORM)) return 0;
@@ -356,7 +358,8 @@ int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_stride_h,
     return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0 (got %d, %lld)", num_seqs,
                 (long long)total_tokens);
   if (num_seqs > 65535) return fail(GDN_ERR_UNSUPPORTED, "num_seqs > 65535 per call is not supported");
-  if (flags) return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_prefill_state_map takes no flags (got 0x%x)", flags);
+  if (flags & ~(GDN_FLAG_STATE_MAP | GDN_PREFILL_SEGMENTS(15)))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_prefill_state_map: unknown flag bits 0x%x", flags);
   if (num_seqs == 0) return ok();
   if (!cu_seqlens || !A_log || !dt_bias || !map_m || !map_c)
     return fail(GDN_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
@@ -369,7 +372,7 @@ int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_stride_h,
         !aligned(v, v_stride_t, v_stride_h, 2, 16))
       return fail(GDN_ERR_UNSUPPORTED, "gdn_prefill_state_map needs 16-byte aligned q/k/v rows (base and strides)");
   }
-  const size_t need = gdn::prefill_chunk_workspace_bytes(num_seqs, total_tokens, num_v_heads, GDN_PREFILL_SEGMENTS(1));
+  const size_t need = gdn::prefill_map_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
   if (need > 0 && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15)))
     return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required (got %zu)", need,
                 workspace_bytes);
@@ -403,7 +406,7 @@ int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_stride_h,
   p.HV = num_v_heads;
   p.ratio = num_v_heads / num_qk_heads;
   p.T = total_tokens;
-  p.flags = GDN_PREFILL_SEGMENTS(1);
+  p.flags = flags;
   p.workspace = workspace;
   p.workspace_bytes = workspace_bytes;
   p.map_m = map_m;

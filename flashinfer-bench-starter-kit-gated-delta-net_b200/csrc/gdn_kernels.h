@@ -115,8 +115,11 @@ int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uin
 bool prefill_chunk_supported(const PrefillParams& p);
 cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream);
 // Per sequence the affine map of its token range, M [HV][K][K] and C [HV][V][K]
-// (S_out = S_in M + C): the chunked chain from the identity with v = 0 and from zero.
+// (S_out = S_in M + C): the chunked chain from the identity with v = 0 and from zero,
+// in prefill_map_segments(...) segments whose maps are then composed.
 cudaError_t launch_prefill_state_map(const PrefillParams& p, cudaStream_t stream);
+int prefill_map_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
+size_t prefill_map_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
 // The maps of empty token ranges: M = I, C = 0 for every sequence and v-head.
 cudaError_t launch_identity_maps(const PrefillParams& p, cudaStream_t stream);
 

@@ -200,11 +200,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   //   2 s - 1 = M of segment s (identity start, v taken as 0), 2 s = C of segment s
   //   (zero start), no outputs (s = 1 .. S - 2).
   // cp_pass 3 (z): segment z + 1 from kCpIn[z], with outputs; the last one ends in p.new_state.
-  // cp_pass 2 (z): the whole sequence's map, 0 = M -> p.map_m, 1 = C -> p.map_c, no outputs.
+  // cp_pass 2 (z): the sequence's map, no outputs: z = 2 s -> M, 2 s + 1 -> C of segment s;
+  //   one segment: straight to p.map_m / p.map_c, else to the map scratch (composed later).
   const int S = p.cp_segments, cz = blockIdx.z;
-  const int seg = p.cp_pass == 1 ? (cz + 1) >> 1 : (p.cp_pass == 3 ? cz + 1 : 0);
+  const int seg = p.cp_pass == 1 ? (cz + 1) >> 1 : (p.cp_pass == 3 ? cz + 1 : (p.cp_pass == 2 ? cz >> 1 : 0));
   const bool emit = p.cp_pass == 0 || p.cp_pass == 3 || (p.cp_pass == 1 && cz == 0);  // outputs written
-  const bool homog = (p.cp_pass == 1 && (cz & 1)) || (p.cp_pass == 2 && cz == 0);     // identity start, v = 0
+  const bool homog = (p.cp_pass == 1 && (cz & 1)) || (p.cp_pass == 2 && !(cz & 1));   // identity start, v = 0
   // where the range's state starts (nullptr: zero, or the identity when homog) and ends
   // (nullptr: not stored); evaluated where used, to keep them out of the loops' registers
   auto init_block = [&]() -> const float* {
@@ -217,8 +218,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       return p.cp_scratch + (cz == 0 ? cp_offset(p.N, p.HV, S, kCpIn, n, 0, h)
                                      : cp_offset(p.N, p.HV, S, (cz & 1) ? kCpMap : kCpOff, n, seg - 1, h));
     if (p.cp_pass == 3 && seg != S - 1) return nullptr;
-    if (p.cp_pass == 2)
-      return cz == 0 ? p.map_m + (size_t)n * p.m_sn + (size_t)h * p.m_sh : p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh;
+    if (p.cp_pass == 2) {
+      if (S > 1) return p.cp_scratch + map_seg_offset(p.N, p.HV, S, cz & 1, n, seg, h);
+      return !(cz & 1) ? p.map_m + (size_t)n * p.m_sn + (size_t)h * p.m_sh : p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh;
+    }
     return p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh;
   };
   const int nch_seq = (int)((seq_len + kC - 1) / kC);
@@ -786,6 +789,48 @@ int device_sm_count() {
 
 }  // namespace
 
+namespace {
+// Composition of segment maps into the map of the whole range: M = M_0 M_1 .. M_{S-1},
+// C = (..((C_0 M_1 + C_1) M_2 + C_2) ..).  z = row block (4) x {M, C}; fp32 CUDA cores.
+__global__ void __launch_bounds__(256) map_combine_kernel(PrefillParams p) {
+  __shared__ __align__(16) float rows[32][kHeadDim];
+  const int h = blockIdx.x, n = blockIdx.y, r0 = (blockIdx.z & 3) * 32, which = blockIdx.z >> 2;
+  const int tid = threadIdx.x, c = tid & 127, rh = (tid >> 7) * 16;
+  const int S = p.cp_segments;
+  const float* first = p.cp_scratch + map_seg_offset(p.N, p.HV, S, which, n, 0, h) + (int64_t)r0 * kHeadDim;
+  for (int e = tid; e < 32 * kHeadDim / 4; e += 256)
+    reinterpret_cast<float4*>(&rows[0][0])[e] = reinterpret_cast<const float4*>(first)[e];
+  __syncthreads();
+  float acc[16];
+  for (int sg = 1; sg < S; ++sg) {
+    const float* M = p.cp_scratch + map_seg_offset(p.N, p.HV, S, 0, n, sg, h);
+    const float* C = p.cp_scratch + map_seg_offset(p.N, p.HV, S, 1, n, sg, h) + (int64_t)r0 * kHeadDim;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = which ? C[(rh + r) * kHeadDim + c] : 0.f;
+#pragma unroll 2
+    for (int k = 0; k < kHeadDim; k += 4) {
+      const float m0 = M[(k + 0) * kHeadDim + c], m1 = M[(k + 1) * kHeadDim + c];
+      const float m2 = M[(k + 2) * kHeadDim + c], m3 = M[(k + 3) * kHeadDim + c];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const float4 x = *reinterpret_cast<const float4*>(&rows[rh + r][k]);
+        acc[r] = fmaf(x.x, m0, acc[r]);
+        acc[r] = fmaf(x.y, m1, acc[r]);
+        acc[r] = fmaf(x.z, m2, acc[r]);
+        acc[r] = fmaf(x.w, m3, acc[r]);
+      }
+    }
+    __syncthreads();  // every thread has read the rows of the previous product
+#pragma unroll
+    for (int r = 0; r < 16; ++r) rows[rh + r][c] = acc[r];
+    __syncthreads();
+  }
+  float* dst = which ? p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh : p.map_m + (size_t)n * p.m_sn + (size_t)h * p.m_sh;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) dst[(int64_t)(r0 + rh + r) * kHeadDim + c] = rows[rh + r][c];
+}
+}  // namespace
+
 cudaError_t launch_prefill_combine(const PrefillParams& p, cudaStream_t stream) {
   if (p.cp_segments < 3) return cudaSuccess;
   prefill_combine_kernel<<<dim3(p.HV, p.N, kHeadDim / 32), 256, 0, stream>>>(p);
@@ -814,6 +859,38 @@ int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uin
     }
   }
   return best <= 0.9 * one ? best_s : 1;
+}
+
+int prefill_map_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  const int req = (int)((flags >> kPrefillSegmentsShift) & 15u);
+  if (req >= 1) return req;
+  // automatic: a map takes two chains per (sequence, v-head) (M and C); S segments of
+  // 1/S of the chunks each take waves(2 c S) segment-lengths against waves(2 c) for one.
+  // The cheapest S in [2, 8] (the smallest on ties) if it saves at least 10 %, for
+  // sequences of 16 chunks or more on average.
+  const int64_t chains = (int64_t)num_seqs * num_v_heads;
+  if (chains <= 0 || total_tokens < (int64_t)num_seqs * 16 * kC) return 1;
+  const int64_t sms = device_sm_count();
+  auto waves = [&](int64_t ctas) { return (double)((ctas + sms - 1) / sms); };
+  const double one = waves(2 * chains);
+  double best = one;
+  int best_s = 1;
+  for (int sg = 2; sg <= 8; ++sg) {
+    const double cost = waves(2 * chains * sg) / sg;
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_s = sg;
+    }
+  }
+  return best <= 0.9 * one ? best_s : 1;
+}
+
+size_t prefill_map_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  if (num_seqs <= 0 || total_tokens <= 0 || num_v_heads <= 0) return 0;
+  const size_t records = (size_t)chunk::num_slots(total_tokens, num_seqs) * (size_t)num_v_heads * chunk::kRecBytes;
+  const int S = prefill_map_segments(num_seqs, total_tokens, num_v_heads, flags);
+  if (S <= 1) return records;
+  return ((records + 255) & ~(size_t)255) + (size_t)2 * S * num_seqs * num_v_heads * kStateFloats * sizeof(float);
 }
 
 size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
@@ -886,14 +963,23 @@ cudaError_t launch_identity_maps(const PrefillParams& p, cudaStream_t stream) {
 cudaError_t launch_prefill_state_map(const PrefillParams& p, cudaStream_t stream) {
   if (p.N == 0) return cudaSuccess;
   PrefillParams q = p;
-  q.cp_segments = 1;
+  const int S = prefill_map_segments(p.N, p.T, p.HV, p.flags);
+  q.cp_segments = S;
   q.cp_pass = 2;
   q.out = nullptr;
   q.new_state = nullptr;
+  if (S > 1) {
+    const size_t records = (size_t)chunk::num_slots(p.T, p.N) * (size_t)p.HV * chunk::kRecBytes;
+    q.cp_scratch =
+        reinterpret_cast<float*>(static_cast<unsigned char*>(p.workspace) + ((records + 255) & ~(size_t)255));
+  }
   CUtensorMap mk, mq, mv, mo;
   cudaError_t e = prefill_setup(q, stream, &mk, &mq, &mv, &mo);
   if (e != cudaSuccess) return e;
-  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2 * S), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || S == 1) return e;
+  map_combine_kernel<<<dim3(p.HV, p.N, 8), 256, 0, stream>>>(q);
   return cudaGetLastError();
 }
 

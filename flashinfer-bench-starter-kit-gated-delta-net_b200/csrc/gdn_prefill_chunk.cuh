@@ -67,6 +67,12 @@ __host__ __device__ inline int64_t cp_offset(int N, int HV, int S, int which, in
   return base + (((int64_t)n * count + idx) * HV + h) * kStateFloats;
 }
 
+// State-map scratch when the map of each sequence is computed in S segments:
+// [2 (M, C)][N][S][HV][128 x 128] fp32.
+__host__ __device__ inline int64_t map_seg_offset(int N, int HV, int S, int which, int n, int sg, int h) {
+  return ((((int64_t)which * N + n) * S + sg) * HV + h) * kStateFloats;
+}
+
 __device__ __forceinline__ int64_t load_cu(const PrefillParams& p, int i) {
   return p.cu_is_int64 ? reinterpret_cast<const int64_t*>(p.cu_seqlens)[i]
                        : (int64_t) reinterpret_cast<const int32_t*>(p.cu_seqlens)[i];

@@ -137,12 +137,17 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, use_qk_l2nor
                    use_qk_l2norm=use_qk_l2norm, serial=serial, segments=segments)
 
 
-def state_map(q, k, v, A_log, a, dt_bias, b, cu_seqlens, map_m=None, map_c=None, *, workspace=None):
+def state_map(q, k, v, A_log, a, dt_bias, b, cu_seqlens, map_m=None, map_c=None, *, workspace=None,
+              segments: int = 0):
     """Affine state map of each sequence's token range (C ABI ``gdn_prefill_state_map``):
     running the range from any initial state S gives ``S_out = S @ M + C`` per
     (sequence, v-head), with ``M`` [N,HV,128,128] the range run from the identity with
-    v taken as 0 and ``C`` [N,HV,128,128] the range run from zero.  No counterpart in
-    the reference; context parallelism composes these maps across ranks."""
+    v taken as 0 and ``C`` [N,HV,128,128] the range run from zero.  ``segments`` cuts
+    each range into that many pieces whose maps are computed on separate SMs and
+    multiplied together (0 = the library decides, 1 = one chain per map).  No
+    counterpart in the reference; context parallelism composes these maps across ranks."""
+    if not 0 <= int(segments) <= 15:
+        raise ValueError(f"segments must be in [0, 15], got {segments}")
     T, HQ, D = q.shape
     HV = v.shape[1]
     N = cu_seqlens.shape[0] - 1
@@ -160,7 +165,8 @@ def state_map(q, k, v, A_log, a, dt_bias, b, cu_seqlens, map_m=None, map_c=None,
     a, b = inner_contig(a), inner_contig(b)
     A_log, dt_bias, cu = A_log.contiguous(), dt_bias.contiguous(), cu_seqlens.contiguous()
     lib = _lib.library()
-    need = int(lib.gdn_prefill_workspace_size(N, T, HQ, HV, D, _lib.GDN_PREFILL_SEGMENTS(1)))
+    flags = _lib.GDN_PREFILL_SEGMENTS(segments)
+    need = int(lib.gdn_prefill_workspace_size(N, T, HQ, HV, D, _lib.GDN_FLAG_STATE_MAP | flags))
     if workspace is None:
         workspace = _workspace(q.device, need)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
@@ -170,6 +176,6 @@ def state_map(q, k, v, A_log, a, dt_bias, b, cu_seqlens, map_m=None, map_c=None,
                                    ptr(cu), int(cu.dtype == torch.int64),
                                    ptr(map_m), *seq_head_strides(map_m, 0, 1),
                                    ptr(map_c), *seq_head_strides(map_c, 0, 1),
-                                   N, T, HQ, HV, D, ptr(workspace), ws_bytes, 0, stream_handle(q.device))
+                                   N, T, HQ, HV, D, ptr(workspace), ws_bytes, flags, stream_handle(q.device))
     _lib.check(rc)
     return map_m, map_c

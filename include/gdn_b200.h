@@ -53,6 +53,8 @@ extern "C" {
  * from their initial states).  0 = automatic (segments only when the (sequence, v-head)
  * chains leave most SMs idle and sequences are long), 1 = never.  Bits 8-11. */
 #define GDN_PREFILL_SEGMENTS(n) ((((uint32_t)(n)) & 15u) << 8)
+/* gdn_prefill_workspace_size: size the workspace of gdn_prefill_state_map instead. */
+#define GDN_FLAG_STATE_MAP 0x4u
 
 /* Device-side error bits reported by gdn_device_error(). */
 #define GDN_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded wait inside a kernel gave up */
@@ -181,12 +183,13 @@ GDN_API int gdn_prefill(const void* q, int64_t q_stride_t, int64_t q_stride_h,
  *   S_out = S M + C      (k-last [V x K] states, row vectors; fp32)
  * with M [K x K] the range run from the identity with v taken as 0 and C [V x K]
  * the range run from a zero state.  Inputs as gdn_prefill (no state, no outputs);
- * q/k/v rows and strides 16-byte aligned.  Writes
+ * q/k/v rows and strides 16-byte aligned.  A long range is cut into segments whose
+ * maps run on separate SMs and are then multiplied together (fp32; flags may carry
+ * GDN_PREFILL_SEGMENTS(n): 0 = automatic, 1 = one chain per map).  Writes
  *   map_m [N, num_v_heads, head_dim, head_dim]   strides (n, h), rows contiguous
  *   map_c [N, num_v_heads, head_dim, head_dim]   strides (n, h), rows contiguous
  * An empty range gives M = I, C = 0.  workspace: at least
- * gdn_prefill_workspace_size(..., GDN_PREFILL_SEGMENTS(1)) bytes, 16-byte aligned.
- * flags must be 0.
+ * gdn_prefill_workspace_size(..., GDN_FLAG_STATE_MAP | flags) bytes, 16-byte aligned.
  */
 GDN_API int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_stride_h,
                 const void* k, int64_t k_stride_t, int64_t k_stride_h,

@@ -118,6 +118,15 @@ def test_workspace_size_with_segments(lib):
     assert lib.gdn_prefill_workspace_size(1, 4096, 16, 32, 128, 0) == rec(1, 4096) + 32 * st * 10
     assert lib.gdn_prefill_workspace_size(1, 512, 16, 32, 128, 0) == rec(1, 512)  # < 16 chunks
     assert lib.gdn_prefill_workspace_size(2, 8192, 16, 32, 128, 0) == rec(2, 8192)  # 64 chains
+    # gdn_prefill_state_map (GDN_FLAG_STATE_MAP): records + [2][N][S][HV] segment maps; one long
+    # 32-head sequence gets S = 2 (128 chains, one wave, half the chunks each)
+    smap = 0x4
+    assert lib.gdn_prefill_workspace_size(1, 4096, 16, 32, 128, smap) == rec(1, 4096) + 2 * 2 * 32 * st
+    assert lib.gdn_prefill_workspace_size(1, 4096, 16, 32, 128, smap | seg(3)) == rec(1, 4096) + 2 * 3 * 32 * st
+    assert lib.gdn_prefill_workspace_size(1, 4096, 16, 32, 128, smap | seg(1)) == rec(1, 4096)
+    # 8 sequences: 512 map chains are 4 waves on 148 SMs, 1024 half-length ones 7 (= 3.5)
+    assert lib.gdn_prefill_workspace_size(8, 8 * 4096, 16, 32, 128, smap) == rec(8, 8 * 4096) + 2 * 2 * 8 * 32 * st
+    assert lib.gdn_prefill_workspace_size(8, 8 * 512, 16, 32, 128, smap) == rec(8, 8 * 512)  # 8 chunks each
 
 
 def test_missing_library_fails_loudly(gdn, monkeypatch, tmp_path):

@@ -24,15 +24,20 @@ HQ, HV = 2, 4
 def test_split_ranges_cover_each_sequence(gdn):
     cp = gdn.context_parallel
     lens = [0, 1, 37, 64, 65, 700, 4096, 130]
-    for world in (1, 2, 3, 4, 8):
-        ranges = cp.split_ranges(lens, world)
-        for i, L in enumerate(lens):
-            spans = [ranges[r][i] for r in range(world)]
-            assert spans[0][0] == 0 and spans[-1][1] == L
-            assert all(x[1] == y[0] for x, y in zip(spans, spans[1:]))
-            assert all(s[0] % 64 == 0 for s in spans)  # every range starts on a chunk boundary
-            sizes = [(e - s + 63) // 64 for s, e in spans]
-            assert max(sizes) - min(sizes) <= 1
+    for weight in (1.0, cp.FIRST_RANK_WEIGHT, 3.0):
+        for world in (1, 2, 3, 4, 8):
+            ranges = cp.split_ranges(lens, world, weight)
+            for i, L in enumerate(lens):
+                spans = [ranges[r][i] for r in range(world)]
+                assert spans[0][0] == 0 and spans[-1][1] == L
+                assert all(x[1] == y[0] for x, y in zip(spans, spans[1:]))
+                assert all(s[0] % 64 == 0 for s in spans)  # every range starts on a chunk boundary
+                sizes = [(e - s + 63) // 64 for s, e in spans]
+                if weight == 1.0:
+                    assert max(sizes) - min(sizes) <= 1
+    # weighted: rank 0 holds first_weight times the chunks of each other rank (to a chunk)
+    r = cp.split_ranges([64 * 280], 4, 1.8)
+    assert [(hi - lo) // 64 for lo, hi in (x[0] for x in r)] == [105, 58, 58, 59]
 
 
 def _bits(t):

@@ -99,8 +99,8 @@ def _oracle_map(inp):
     return m, c
 
 
-@pytest.mark.parametrize("slow_decay", [False, True])
-def test_state_map_matches_oracle_and_is_affine(gdn, slow_decay):
+@pytest.mark.parametrize("slow_decay,segments", [(False, 0), (True, 0), (True, 3)])
+def test_state_map_matches_oracle_and_is_affine(gdn, slow_decay, segments):
     """M = the range from the identity with v = 0, C = the range from zero; and the
     prefill from any state S ends in S M + C.  With the benchmark gates the state
     forgets its start within tens of tokens (M falls to 1e-18 .. 1e-38 on the short
@@ -113,7 +113,7 @@ def test_state_map_matches_oracle_and_is_affine(gdn, slow_decay):
         inp["A_log"] = torch.full_like(inp["A_log"], -6.0)
     dev = to_dev(inp)
     M, C = gdn.kernel_prefill.state_map(dev["q"], dev["k"], dev["v"], dev["A_log"], dev["a"], dev["dt_bias"],
-                                        dev["b"], dev["cu_seqlens"])
+                                        dev["b"], dev["cu_seqlens"], segments=segments)
     torch.cuda.synchronize()
     m_ref, c_ref = _oracle_map(inp)
     ok, err = state_close(C[1:].cpu().numpy(), c_ref[1:], 1e-3)
@@ -129,6 +129,28 @@ def test_state_map_matches_oracle_and_is_affine(gdn, slow_decay):
     torch.cuda.synchronize()
     ok, err = state_close(comp.cpu().numpy(), fin.cpu().numpy(), 1e-4)
     assert ok, err
+
+
+def test_state_map_automatic_segments_one_long_sequence(gdn):
+    """One sequence, 32 v-heads: the map is computed in segments (the workspace grows
+    by their maps), multiplied on the GPU; slow decay keeps M far from zero."""
+    T = 64 * 40 + 5
+    inp = gdn.workloads.prefill_inputs([T], seed=335)
+    inp["A_log"] = torch.full_like(inp["A_log"], -6.0)
+    lib = gdn._lib.library()
+    records = (T // 64 + 2) * 32 * 17664
+    assert lib.gdn_prefill_workspace_size(1, T, 16, 32, 128, gdn._lib.GDN_FLAG_STATE_MAP) > records
+    dev = to_dev(inp)
+    M, C = gdn.kernel_prefill.state_map(dev["q"], dev["k"], dev["v"], dev["A_log"], dev["a"], dev["dt_bias"],
+                                        dev["b"], dev["cu_seqlens"])
+    M1, C1 = gdn.kernel_prefill.state_map(dev["q"], dev["k"], dev["v"], dev["A_log"], dev["a"], dev["dt_bias"],
+                                          dev["b"], dev["cu_seqlens"], segments=1)
+    torch.cuda.synchronize()
+    m_ref, c_ref = _oracle_map(inp)
+    for got in ((M, C), (M1, C1)):
+        for g_, w_ in zip(got, (m_ref, c_ref)):
+            ok, err = state_close(g_.cpu().numpy(), w_, 1e-3)
+            assert ok, err
 
 
 def test_context_parallel_steps_on_one_gpu(gdn):
