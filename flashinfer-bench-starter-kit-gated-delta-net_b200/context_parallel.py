@@ -23,11 +23,14 @@ reference has no long-context parallelism (its prefill is token-serial per
 sequence, ``solution/triton/kernel_prefill.py:88``).
 
 ``split_ranges``/``local_inputs`` cut a global varlen batch into rank-local inputs:
-every range of a sequence starts on a 64-token chunk boundary.  Rank 0 does one pass
-over its range and every other rank two (map, rerun), so rank 0's range is weighted
-``FIRST_RANK_WEIGHT`` times the others' by default: with the in-GPU segments of one
-long 32-head sequence a prefill costs ~0.6 and a map ~0.5 of one chain per token, so
-(0.5 + 0.6) / 0.6 ≈ 1.8.
+every range of a sequence starts on a 64-token chunk boundary.  The reruns need the
+state leaving rank 0's range, so rank 0's prefill and the other ranks' maps form the
+first stage of the critical path and the reruns the second: rank 0's range is weighted
+``FIRST_RANK_WEIGHT`` times the others' so that its prefill ends with their maps (with
+the in-GPU segments of one long 32-head sequence a map costs ~0.5 and a prefill ~0.6
+of one chain per token: 0.5 / 0.6 ≈ 0.8).  A step then takes ~1.1 range-lengths of one
+chain on each rank against ~0.6 sequence-lengths on one GPU: about even at 2 ranks,
+~2x at 4, ~4x at 8.
 """
 from __future__ import annotations
 
@@ -38,7 +41,7 @@ import torch
 import torch.distributed as dist
 
 CHUNK = 64
-FIRST_RANK_WEIGHT = 1.8
+FIRST_RANK_WEIGHT = 0.8
 
 
 def split_ranges(seqlens, world: int, first_weight: float = FIRST_RANK_WEIGHT) -> list[list[tuple[int, int]]]:

@@ -36,8 +36,8 @@ def test_split_ranges_cover_each_sequence(gdn):
                 if weight == 1.0:
                     assert max(sizes) - min(sizes) <= 1
     # weighted: rank 0 holds first_weight times the chunks of each other rank (to a chunk)
-    r = cp.split_ranges([64 * 280], 4, 1.8)
-    assert [(hi - lo) // 64 for lo, hi in (x[0] for x in r)] == [105, 58, 58, 59]
+    r = cp.split_ranges([64 * 380], 4, 0.8)
+    assert [(hi - lo) // 64 for lo, hi in (x[0] for x in r)] == [80, 100, 100, 100]
 
 
 def _bits(t):
