@@ -61,7 +61,7 @@ constexpr int kWarpP0 = kChainWarps;  // P warpgroup: 4 warps after the chain wa
 constexpr int kWarpTma = kChainWarps + 4, kWarpMma = kChainWarps + 5;
 constexpr int kThreads = 32 * (kChainWarps + 6);
 constexpr int kStateCols = 128 / kCW, kTokCols = 64 / kCW;  // per chain thread
-static_assert(kCW == 2 || kCW == 4, "chain split");
+static_assert(kCW == 4, "chain split: a chain thread holds 32 state columns");
 constexpr uint32_t kTmemCols = 512;
 
 // TMEM column map (lanes = state row v unless noted)
@@ -157,6 +157,34 @@ __device__ __forceinline__ bool wait_bar(const Smem& sm, uint64_t* bar, uint32_t
   }
 }
 
+// Longest chains first.  CTAs start in blockIdx order, so blockIdx.y is mapped to
+// the sequences by decreasing length (ties: lower index first): the long chains
+// start in the first wave and the short ones fill the tail of the last.  `rank`
+// < N; the ranks of a strict total order are a permutation, so exactly one
+// thread finds it.  Up to kLptMaxSeqs sequences (each thread ranks one sequence
+// against all others); above that the identity order is kept.
+constexpr int kLptMaxSeqs = 128;
+__device__ int lpt_sequence(const PrefillParams& p, int rank, unsigned char* scratch) {
+  if (p.N <= 1 || p.N > kLptMaxSeqs) return rank;
+  int64_t* len = reinterpret_cast<int64_t*>(scratch);
+  int* pick = reinterpret_cast<int*>(scratch + kLptMaxSeqs * sizeof(int64_t));
+  const int tid = threadIdx.x;
+  if (tid < p.N) len[tid] = load_cu(p, tid + 1) - load_cu(p, tid);
+  __syncthreads();
+  if (tid < p.N) {
+    const int64_t mine = len[tid];
+    int r = 0;
+#pragma unroll 4
+    for (int m = 0; m < p.N; ++m) {
+      const int64_t o = len[m];
+      r += (o > mine || (o == mine && m < tid)) ? 1 : 0;
+    }
+    if (r == rank) *pick = tid;
+  }
+  __syncthreads();
+  return *pick;
+}
+
 // Wait of a group of `n` threads: the leader polls the mbarrier, then the group
 // meets at named barrier `bar_id` and AND-reduces the outcome, so all threads
 // either proceed or leave together.
@@ -185,7 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem sm;
   sm.base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-  const int h = blockIdx.x, n = blockIdx.y;
+  const int h = blockIdx.x;
+  const int n = lpt_sequence(p, blockIdx.y, sm.base + kSmO);  // the output stage is free until the first chunk
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qh = h / p.ratio;
 
@@ -555,19 +584,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t d1 = kTmD1 + (uint32_t)s * 128;
       if (!group_wait(sm, B_GATES + s, (i >> 1) & 1, 1, kChainThreads, leader)) break;
       const float GC = sm.gate(s, GA_G)[63];
-      // ---- S0 hi/lo into TMEM (A of the first MMA) ----
+      // ---- S0 hi/lo into TMEM (A of the first MMA): the thread's 32 state columns in one
+      //      load, kept in registers for the G_C scaling below ----
       if (i > 0 && !group_wait(sm, B_MMA4 + ((i - 1) & 1), ((i - 1) >> 1) & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
+      float xs[kStateCols];
+      tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, kTmS + sc), xs);
+      tc::tmem_wait_ld();
 #pragma unroll
-      for (int piece = 0; piece < kStateCols / 16; ++piece) {
-        float x[16];
-        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, kTmS + sc + piece * 16), x);
-        tc::tmem_wait_ld();
+      for (int half = 0; half < 2; ++half) {
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) split2(x[2 * u], x[2 * u + 1], hi[u], lo[u]);
-        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmS0hi + sc / 2 + piece * 8), hi);
-        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmS0lo + sc / 2 + piece * 8), lo);
+        for (int u = 0; u < 8; ++u) split2(xs[16 * half + 2 * u], xs[16 * half + 2 * u + 1], hi[u], lo[u]);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmS0hi + sc / 2 + half * 8), hi);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmS0lo + sc / 2 + half * 8), lo);
       }
       tc::tmem_wait_st();
       tc::fence_before_sync();
@@ -576,15 +606,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- S <- G_C * S while the first MMA runs (it reads only the hi/lo copies; the
       //      state MMA of this chunk comes after the deltas) ----
 #pragma unroll
-      for (int piece = 0; piece < kStateCols / 16; ++piece) {
-        float x[16];
-        const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + sc + piece * 16);
-        tc::tmem_ld16(ta, x);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int q = 0; q < 16; ++q) x[q] *= GC;
-        tc::tmem_st16(ta, x);
-      }
+      for (int q = 0; q < kStateCols; ++q) xs[q] *= GC;
+      tc::tmem_st32(tc::tmem_addr(tmem, lane_base, kTmS + sc), xs);
       tc::tmem_wait_st();
       // ---- R^T = beta V^T - beta G (S0 K^T), split hi/lo into TMEM (16 token columns per thread) ----
       if (!group_wait(sm, B_V_FULL, i & 1, 1, kChainThreads, leader)) break;

@@ -37,15 +37,21 @@ constexpr int kLd = 68;  // padded row stride (floats) of the in-place A / T arr
 
 constexpr uint32_t kSmK = 0;            // 2 tiles (feature cols 0-63 | 64-127) x [128 rows x 128 B]
 constexpr uint32_t kKTile = 16384;
-constexpr uint32_t kSmAT = 32768;       // per group: A, then T, in place [64][kLd] fp32
+// per group: A, then T, in place [64][kLd] fp32.  It overlays the K tiles: A is written
+// only after the K K^T products have completed (their commit barrier), when no
+// tcgen05 read of the tiles is left.
+constexpr uint32_t kSmAT = 0;
 constexpr uint32_t kATBytes = 64 * kLd * 4;
 constexpr uint32_t kSmGate = kSmAT + 2 * kATBytes;  // per group: GA_N x 64 fp32 + scan scratch
 constexpr uint32_t kGateBytes = (GA_N + 1) * 64 * 4;
 constexpr uint32_t kSmBar = kSmGate + 2 * kGateBytes;
 constexpr uint32_t kSmMisc = kSmBar + 16;  // tmem base slot, per-group chunk info
 constexpr uint32_t kSmBytes = kSmMisc + 80;
-constexpr uint32_t kSmAlloc = kSmBytes + 1024;
-static_assert(kSmAlloc * 3 <= 227 * 1024, "three CTAs per SM");
+// Four CTAs per SM (64 registers, 128 TMEM columns each).  The allocation is padded
+// so that a fifth cannot become resident and wait on TMEM (5 x 47 KB > 228 KB).
+constexpr uint32_t kSmAlloc = (kSmBytes + 1024) > 46 * 1024 ? (kSmBytes + 1024) : 46 * 1024;
+static_assert(kSmK + 2 * kKTile <= kSmGate && kSmAT + 2 * kATBytes <= kSmGate, "smem map");
+static_assert((kSmAlloc + 1024) * 4 <= 228 * 1024 && (kSmAlloc + 1024) * 5 > 228 * 1024, "four CTAs per SM");
 
 struct SlotInfo {
   int64_t slot;
@@ -218,7 +224,7 @@ __device__ __forceinline__ void solve_merge32(float* AT, int p, int bar) {
   named_sync(bar, 128);
 }
 
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, 4)
     prefill_prep_kernel(const __grid_constant__ CUtensorMap mapK, PrefillParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base =
