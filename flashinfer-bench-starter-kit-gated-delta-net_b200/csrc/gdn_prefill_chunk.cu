@@ -119,6 +119,7 @@ enum : int {
   B_D_READY,
   B_MMA3,
   B_P_READY,        // P tile written and S0 Q^T scaled by G
+  B_DTILE,          // D^T bf16 tile written (A of the output MMA)
   B_DRAIN,
   B_COUNT
 };
@@ -401,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mma_commit(sm.bar(B_MMA4 + s));
         tc::mma_commit(sm.bar(B_KQ_EMPTY + s));
         if (!wait_bar(sm, sm.bar(B_P_READY), i & 1)) break;
+        if (!wait_bar(sm, sm.bar(B_DTILE), i & 1)) break;
         tc::fence_after_sync();
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
@@ -609,40 +611,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int q = 0; q < kStateCols; ++q) xs[q] *= GC;
       tc::tmem_st32(tc::tmem_addr(tmem, lane_base, kTmS + sc), xs);
       tc::tmem_wait_st();
-      // ---- R^T = beta V^T - beta G (S0 K^T), split hi/lo into TMEM (16 token columns per thread) ----
+      // ---- while the first MMA runs: beta_t V[t][v] and beta_t G_t of this thread's 16 token
+      //      columns, and the state-update decays exp(g_C - g_t), into registers ----
+      static_assert(kTokCols == 16, "one 16-token piece per chain thread");
       if (!group_wait(sm, B_V_FULL, i & 1, 1, kChainThreads, leader)) break;
+      float bv[16], bgx[16], rdec[16];
+      {
+        const float* bet = sm.gate(s, GA_BETA) + tb;
+        const float* bg = sm.gate(s, GA_BG) + tb;
+        const float* rr = sm.gate(s, GA_R) + tb;
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(bet + 4 * u4);
+          const float4 g4 = *reinterpret_cast<const float4*>(bg + 4 * u4);
+          const float4 r4 = *reinterpret_cast<const float4*>(rr + 4 * u4);
+          const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, gg[4] = {g4.x, g4.y, g4.z, g4.w};
+          const float rq[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int u = 4 * u4 + e;
+            // a state map's homogeneous part takes v as 0
+            bv[u] = homog ? 0.f : bb[e] * __bfloat162float(vt[(tb + u) * kHeadDim + v]);
+            bgx[u] = gg[e];
+            rdec[u] = rq[e];
+          }
+        }
+      }
+      // ---- R^T = beta V^T - beta G (S0 K^T), split hi/lo into TMEM ----
       if (!group_wait(sm, B_MMA1, i & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
-#pragma unroll
-      for (int piece = 0; piece < kTokCols / 16; ++piece) {
-        const int t0c = tb + piece * 16;
+      {
         float x[16];
-        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, d1 + 64 + t0c), x);
-        float vv[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u) vv[u] = __bfloat162float(vt[(t0c + u) * kHeadDim + v]);
-        const float* bet = sm.gate(s, GA_BETA) + t0c;
-        const float vmul = homog ? 0.f : 1.f;  // a state map's homogeneous part: v taken as 0
-        const float* bg = sm.gate(s, GA_BG) + t0c;
+        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, d1 + 64 + tb), x);
         tc::tmem_wait_ld();
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int u4 = 0; u4 < 4; ++u4) {
-          float4 b4 = *reinterpret_cast<const float4*>(bet + 4 * u4);
-          b4.x *= vmul;
-          b4.y *= vmul;
-          b4.z *= vmul;
-          b4.w *= vmul;
-          const float4 g4 = *reinterpret_cast<const float4*>(bg + 4 * u4);
-          const float r0 = fmaf(b4.x, vv[4 * u4 + 0], -g4.x * x[4 * u4 + 0]);
-          const float r1 = fmaf(b4.y, vv[4 * u4 + 1], -g4.y * x[4 * u4 + 1]);
-          const float r2 = fmaf(b4.z, vv[4 * u4 + 2], -g4.z * x[4 * u4 + 2]);
-          const float r3 = fmaf(b4.w, vv[4 * u4 + 3], -g4.w * x[4 * u4 + 3]);
-          split2(r0, r1, hi[2 * u4], lo[2 * u4]);
-          split2(r2, r3, hi[2 * u4 + 1], lo[2 * u4 + 1]);
-        }
-        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRhi + t0c / 2), hi);
-        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRlo + t0c / 2), lo);
+        for (int u = 0; u < 8; ++u)
+          split2(fmaf(-bgx[2 * u], x[2 * u], bv[2 * u]), fmaf(-bgx[2 * u + 1], x[2 * u + 1], bv[2 * u + 1]), hi[u],
+                 lo[u]);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRhi + tb / 2), hi);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRlo + tb / 2), lo);
       }
       tc::tmem_wait_st();
       tc::fence_before_sync();
@@ -651,43 +659,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(sm.bar(B_R_READY));
         mbar_arrive(sm.bar(B_V_EMPTY));
       }
-      // ---- deltas: D^T (bf16 tile, output MMA) and Dt^T = D^T exp(gC - g) (hi/lo into TMEM, state MMA) ----
+      // ---- deltas: Dt^T = D^T exp(gC - g) (hi/lo into TMEM, state MMA) first; then D^T as a
+      //      bf16 tile for the output MMA, after the state MMA has been released ----
       if (!group_wait(sm, B_MMA2, i & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
-#pragma unroll
-      for (int piece = 0; piece < kTokCols / 16; ++piece) {
-        const int t0c = tb + piece * 16;
-        float d[16];
-        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, d1 + 64 + t0c), d);
-        const float* rr = sm.gate(s, GA_R) + t0c;
+      float d[16];
+      {
+        tc::tmem_ld16(tc::tmem_addr(tmem, lane_base, d1 + 64 + tb), d);
         tc::tmem_wait_ld();
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int c8 = 0; c8 < 2; ++c8) {
-          uint4 dd;
-          dd.x = pack_bf16x2(d[8 * c8 + 0], d[8 * c8 + 1]);
-          dd.y = pack_bf16x2(d[8 * c8 + 2], d[8 * c8 + 3]);
-          dd.z = pack_bf16x2(d[8 * c8 + 4], d[8 * c8 + 5]);
-          dd.w = pack_bf16x2(d[8 * c8 + 6], d[8 * c8 + 7]);
-          st_tile(dtile, v, (t0c >> 3) + c8, dd);
-          const float4 r0 = *reinterpret_cast<const float4*>(rr + 8 * c8);
-          const float4 r1 = *reinterpret_cast<const float4*>(rr + 8 * c8 + 4);
-          split2(d[8 * c8 + 0] * r0.x, d[8 * c8 + 1] * r0.y, hi[4 * c8 + 0], lo[4 * c8 + 0]);
-          split2(d[8 * c8 + 2] * r0.z, d[8 * c8 + 3] * r0.w, hi[4 * c8 + 1], lo[4 * c8 + 1]);
-          split2(d[8 * c8 + 4] * r1.x, d[8 * c8 + 5] * r1.y, hi[4 * c8 + 2], lo[4 * c8 + 2]);
-          split2(d[8 * c8 + 6] * r1.z, d[8 * c8 + 7] * r1.w, hi[4 * c8 + 3], lo[4 * c8 + 3]);
-        }
-        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDthi + t0c / 2), hi);
-        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDtlo + t0c / 2), lo);
+        for (int u = 0; u < 8; ++u) split2(d[2 * u] * rdec[2 * u], d[2 * u + 1] * rdec[2 * u + 1], hi[u], lo[u]);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDthi + tb / 2), hi);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDtlo + tb / 2), lo);
       }
       tc::tmem_wait_st();
-      tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       named_sync(1, kChainThreads);
       if (leader) {
         mbar_arrive(sm.bar(B_D_READY));
         mbar_arrive(sm.bar(B_GFREE + s));
       }
+      // the output MMA of chunk i - 1 (which read the tile) completed before MMA2 of chunk i
+#pragma unroll
+      for (int c8 = 0; c8 < 2; ++c8) {
+        uint4 dd;
+        dd.x = pack_bf16x2(d[8 * c8 + 0], d[8 * c8 + 1]);
+        dd.y = pack_bf16x2(d[8 * c8 + 2], d[8 * c8 + 3]);
+        dd.z = pack_bf16x2(d[8 * c8 + 4], d[8 * c8 + 5]);
+        dd.w = pack_bf16x2(d[8 * c8 + 6], d[8 * c8 + 7]);
+        st_tile(dtile, v, (tb >> 3) + c8, dd);
+      }
+      tc::fence_proxy_async_smem();
+      named_sync(1, kChainThreads);
+      if (leader) mbar_arrive(sm.bar(B_DTILE));
     }
     // ---- final state ----
     bool ok = true;
