@@ -106,13 +106,14 @@ enum : int {
   B_GFREE = 6,      // [2] chain and P warpgroup are done with a gate stage (2 arrivals)
   B_T_FULL = 8,     // [2] T record landed
   B_T_EMPTY = 10,   // [2] the MMA reading a T stage has completed
-  B_OUT_DONE = 12,  // [2] outputs of a chunk read out of D1 buffer (chunk & 1)
+  B_OUT_UNUSED = 12,  // [2] (unused)
   B_MMA4 = 14,      // [2] state update of a chunk done (per chunk parity)
   B_KKQK = 16,      // [K; Q] K^T of a chunk is in its D1 buffer, columns 0-63
-  B_D0_FREE,        // P warpgroup has read that Q K^T
+  B_D0_UNUSED,      // (unused)
   B_V_FULL,
   B_V_EMPTY,
-  B_S0_READY,
+  B_S0_READY,       // MMA1 may go: S0 hi/lo written (chain) and the P warpgroup has read the Q K^T
+                    // of the chunk's D1 buffer (having stored the outputs of chunk i - 2 from it)
   B_MMA1,
   B_R_READY,        // R written (also: S0 Q^T may be scaled by the P warpgroup from here on)
   B_MMA2,
@@ -262,7 +263,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t slot0 = slot_start(cu0, n) + cb;  // workspace record slot of the range's chunk 0
 
   if (tid == 0) {
-    for (int i = 0; i < B_COUNT; ++i) mbar_init(sm.bar(i), (i == B_GFREE || i == B_GFREE + 1) ? 2 : 1);
+    for (int i = 0; i < B_COUNT; ++i)
+      mbar_init(sm.bar(i), (i == B_GFREE || i == B_GFREE + 1 || i == B_S0_READY) ? 2 : 1);
     *sm.abort_flag() = 0;
     fence_barrier_init();
   }
@@ -340,30 +342,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t dKmn0 = tc::mnmajor_desc(sm.addr(kSmKQ + kRowsK), kKQTile, 0);
       const uint64_t dKmn1 = tc::mnmajor_desc(sm.addr(kSmKQ + kKQStage + kRowsK), kKQTile, 0);
       constexpr uint64_t kOffQ2 = kRowsQ2 >> 4, kOffK = kRowsK >> 4;  // descriptor offsets of the [Q; K] and K rows
-      // [Q; Q] K^T of chunk j into D1[j & 1] columns 64-127 (Q K^T on lanes 0-63 and again on
-      // 64-127); that half of the buffer was last read by the deltas of chunk j - 2
-      auto issue_kkqk = [&](int j) -> bool {
-        if (!wait_bar(sm, sm.bar(B_KQ_FULL + (j & 1)), (j >> 1) & 1)) return false;
-        tc::fence_after_sync();
+      // [Q; Q] K^T of chunk j goes into D1[j & 1] columns 64-127 (Q K^T on lanes 0-63 and again
+      // on 64-127); that half of the buffer was last read by the deltas of chunk j - 2
+      // [Q; Q] K^T steps k0 .. k1 - 1 of chunk j (K = 128 in 8 steps of 16)
+      auto kk_steps = [&](int j, int k0, int k1) {
         const uint64_t d = (j & 1) ? dKQ1 : dKQ0;
         const uint32_t dst = tmem + kTmD1 + (uint32_t)(j & 1) * 128 + 64;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          tc::mma_bf16(dst, d + kmajor_step(kKQTile, ks), d + kOffK + kmajor_step(kKQTile, ks), id_n64, ks > 0);
-        tc::mma_commit(sm.bar(B_KKQK));
-        return true;
+          if (ks >= k0 && ks < k1)
+            tc::mma_bf16(dst, d + kmajor_step(kKQTile, ks), d + kOffK + kmajor_step(kKQTile, ks), id_n64, ks > 0);
       };
-      bool ok = issue_kkqk(0);
+      bool ok = wait_bar(sm, sm.bar(B_KQ_FULL), 0);
+      if (ok) {
+        tc::fence_after_sync();
+        kk_steps(0, 0, 8);
+        tc::mma_commit(sm.bar(B_KKQK));
+      }
+      // Probes of a barrier cost this thread several hundred cycles even when its phase is
+      // complete, and the thread issues every MMA of the chain, so the waits on its critical
+      // path are kept to one per MMA group: the T record is checked while the chain splits S0,
+      // and MMA1's two preconditions (S0 split, Q K^T read by the P warpgroup) share a barrier.
       for (int i = 0; ok && i < nchunks; ++i) {
         const int s = i & 1;
         const uint64_t dK = s ? dKQ1 : dKQ0;
         const uint64_t dKmn = s ? dKmn1 : dKmn0;
         const uint32_t d1 = tmem + kTmD1 + (uint32_t)s * 128;
-        // MMA1: D1 = S0_hi [Q; K]^T (N = 128), then D1[:, K part] += S0_lo K^T; the buffer's
-        // Q K^T has been read and its outputs of chunk i - 2 stored
+        if (!wait_bar(sm, sm.bar(B_T_FULL + s), (i >> 1) & 1)) break;
+        // MMA1: D1 = S0_hi [Q; K]^T (N = 128), then D1[:, K part] += S0_lo K^T
         if (!wait_bar(sm, sm.bar(B_S0_READY), i & 1)) break;
-        if (!wait_bar(sm, sm.bar(B_D0_FREE), i & 1)) break;
-        if (i >= 2 && !wait_bar(sm, sm.bar(B_OUT_DONE + s), ((i - 2) >> 1) & 1)) break;
         tc::fence_after_sync();
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
@@ -372,10 +379,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < 8; ++ks)
           tc::mma_bf16_ta(d1 + 64, tmem + kTmS0lo + 8 * ks, dK + kOffK + kmajor_step(kKQTile, ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA1));
-        // next chunk's Q K^T while the chain computes R
-        if (i + 1 < nchunks && !issue_kkqk(i + 1)) break;
+        // the next chunk's Q K^T in two halves, in the tensor pipe's idle windows: while the
+        // chain computes R and while it computes the deltas
+        const bool more = i + 1 < nchunks;
+        if (more) {
+          if (!wait_bar(sm, sm.bar(B_KQ_FULL + ((i + 1) & 1)), ((i + 1) >> 1) & 1)) break;
+          tc::fence_after_sync();
+          kk_steps(i + 1, 0, 4);
+        }
         // MMA2: D^T = R^T T^T into D1 columns 64-127 (R and T split hi/lo: 3 products)
-        if (!wait_bar(sm, sm.bar(B_T_FULL + s), (i >> 1) & 1)) break;
         if (!wait_bar(sm, sm.bar(B_R_READY), i & 1)) break;
         tc::fence_after_sync();
         const uint64_t dT = s ? dT1 : dT0;
@@ -390,6 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::mma_bf16_ta(d1 + 64, tmem + kTmRhi + 8 * ks, dT + kTlo + kmajor_step(0, ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA2));
         tc::mma_commit(sm.bar(B_T_EMPTY + s));
+        if (more) {
+          kk_steps(i + 1, 4, 8);
+          tc::mma_commit(sm.bar(B_KKQK));
+        }
         // state first: S += Dt^T K (hi/lo); then the output: D1[:, O part] += D^T P^T
         if (!wait_bar(sm, sm.bar(B_D_READY), i & 1)) break;
         tc::fence_after_sync();
@@ -440,7 +456,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_before_sync();
       tc::fence_proxy_async_smem();
       named_sync(2, 128);
-      if (pleader) mbar_arrive(sm.bar(B_OUT_DONE + (ci & 1)));
       if (warp == kWarpP0 && emit) {
         if (nvalid == kC) {  // whole chunk: one tiled store of the [64 x 128] box
           if (lane == 0) tc::tma_store_3d(&mapO, 0, h, (int)(t0 + (int64_t)ci * kC), ostage);
@@ -494,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::fence_before_sync();
       named_sync(2, 128);
-      if (pleader) mbar_arrive(sm.bar(B_D0_FREE));
+      if (pleader) mbar_arrive(sm.bar(B_S0_READY));  // this chunk's Q K^T has been read
       // ---- P tile, once the output MMA of chunk i-1 has read the previous one ----
       if (i >= 1 && !group_wait(sm, B_MMA3, (i - 1) & 1, 2, 128, pleader)) break;
       {
