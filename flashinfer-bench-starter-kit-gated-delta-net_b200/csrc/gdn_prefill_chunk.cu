@@ -102,9 +102,9 @@ static_assert(kSmAlloc <= 232448, "smem budget");
 enum : int {
   B_KQ_FULL = 0,    // [2]
   B_KQ_EMPTY = 2,   // [2]
-  B_GATES = 4,      // [2] gate record landed
+  B_REC_FULL = 4,   // [2] record landed: T (hi | lo) and the gate arrays (one expect_tx, two copies)
   B_GFREE = 6,      // [2] chain and P warpgroup are done with a gate stage (2 arrivals)
-  B_T_FULL = 8,     // [2] T record landed
+  B_T_UNUSED = 8,   // [2] (unused)
   B_T_EMPTY = 10,   // [2] the MMA reading a T stage has completed
   B_OUT_UNUSED = 12,  // [2] (unused)
   B_MMA4 = 14,      // [2] state update of a chunk done (per chunk parity)
@@ -117,9 +117,10 @@ enum : int {
   B_MMA1,
   B_R_READY,        // R written (also: S0 Q^T may be scaled by the P warpgroup from here on)
   B_MMA2,
-  B_D_READY,
+  B_D_READY,        // MMA4 may go: Dt hi/lo written (chain), and the P warpgroup has written the
+                    // P tile and scaled S0 Q^T (so the output MMA after MMA4 needs only the D^T tile)
   B_MMA3,
-  B_P_READY,        // P tile written and S0 Q^T scaled by G
+  B_P_UNUSED,       // (unused)
   B_DTILE,          // D^T bf16 tile written (A of the output MMA)
   B_DRAIN,
   B_COUNT
@@ -264,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < B_COUNT; ++i)
-      mbar_init(sm.bar(i), (i == B_GFREE || i == B_GFREE + 1 || i == B_S0_READY) ? 2 : 1);
+      mbar_init(sm.bar(i), (i == B_GFREE || i == B_GFREE + 1 || i == B_S0_READY || i == B_D_READY) ? 2 : 1);
     *sm.abort_flag() = 0;
     fence_barrier_init();
   }
@@ -290,13 +291,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = ((i - 2) >> 1) & 1;  // phase of this stage's previous use (chunk i - 2)
         const int z = (int)(t0 + (int64_t)i * kC);
         const unsigned char* rec = record(p, slot0 + i, h);
-        // waits in the order their phases complete: MMA2(i-2), deltas(i-2), MMA4(i-2), R(i-1)
+        // waits in the order their phases complete: MMA2(i-2), deltas(i-2), MMA4(i-2), R(i-1).
+        // One barrier counts both parts of the record (its phase completes once both landed).
         if (i >= 2 && !wait_bar(sm, sm.bar(B_T_EMPTY + s), ph)) break;
-        mbar_arrive_expect_tx(sm.bar(B_T_FULL + s), kRecT);
-        bulk_g2s(sm.base + kSmT + s * kTStage, rec, kRecT, sm.bar(B_T_FULL + s));
+        mbar_arrive_expect_tx(sm.bar(B_REC_FULL + s), kRecBytes);
+        bulk_g2s(sm.base + kSmT + s * kTStage, rec, kRecT, sm.bar(B_REC_FULL + s));
         if (i >= 2 && !wait_bar(sm, sm.bar(B_GFREE + s), ph)) break;
-        mbar_arrive_expect_tx(sm.bar(B_GATES + s), kRecGates);
-        bulk_g2s(sm.base + kSmGate + s * kRecGates, rec + kRecT, kRecGates, sm.bar(B_GATES + s));
+        bulk_g2s(sm.base + kSmGate + s * kRecGates, rec + kRecT, kRecGates, sm.bar(B_REC_FULL + s));
         if (i >= 2 && !wait_bar(sm, sm.bar(B_KQ_EMPTY + s), ph)) break;
         uint64_t* full = sm.bar(B_KQ_FULL + s);
         mbar_arrive_expect_tx(full, 6 * 8192);
@@ -315,8 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // drain: the last loads have landed before the CTA can exit (bounded)
       if (issued > 0) {
         const int i = issued - 1, s = i & 1;
-        wait_bar(sm, sm.bar(B_T_FULL + s), (i >> 1) & 1);
-        wait_bar(sm, sm.bar(B_GATES + s), (i >> 1) & 1);
+        wait_bar(sm, sm.bar(B_REC_FULL + s), (i >> 1) & 1);
         wait_bar(sm, sm.bar(B_KQ_FULL + s), (i >> 1) & 1);
         wait_bar(sm, sm.bar(B_V_FULL), i & 1);
       }
@@ -361,14 +361,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Probes of a barrier cost this thread several hundred cycles even when its phase is
       // complete, and the thread issues every MMA of the chain, so the waits on its critical
-      // path are kept to one per MMA group: the T record is checked while the chain splits S0,
-      // and MMA1's two preconditions (S0 split, Q K^T read by the P warpgroup) share a barrier.
+      // path are kept to one per MMA group: the preconditions of MMA1 (S0 split, Q K^T read by
+      // the P warpgroup) share a barrier, and so do those of MMA4 and the output MMA (deltas,
+      // P tile); the T record is covered by the chain's wait on the record before its split.
       for (int i = 0; ok && i < nchunks; ++i) {
         const int s = i & 1;
         const uint64_t dK = s ? dKQ1 : dKQ0;
         const uint64_t dKmn = s ? dKmn1 : dKmn0;
         const uint32_t d1 = tmem + kTmD1 + (uint32_t)s * 128;
-        if (!wait_bar(sm, sm.bar(B_T_FULL + s), (i >> 1) & 1)) break;
         // MMA1: D1 = S0_hi [Q; K]^T (N = 128), then D1[:, K part] += S0_lo K^T
         if (!wait_bar(sm, sm.bar(B_S0_READY), i & 1)) break;
         tc::fence_after_sync();
@@ -417,7 +417,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::mma_bf16_ta(tmem + kTmS, tmem + kTmDtlo + 8 * ks, dKmn + mnmajor_step(ks), id_st, true);
         tc::mma_commit(sm.bar(B_MMA4 + s));
         tc::mma_commit(sm.bar(B_KQ_EMPTY + s));
-        if (!wait_bar(sm, sm.bar(B_P_READY), i & 1)) break;
         if (!wait_bar(sm, sm.bar(B_DTILE), i & 1)) break;
         tc::fence_after_sync();
 #pragma unroll
@@ -472,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t d1 = kTmD1 + (uint32_t)s * 128;
       // ---- P rows from Q K^T (warps 10, 11: TMEM lanes 64-127), kept in registers until the
       //      P tile is free: P[t][j] = exp(g_t - g_j) q_t.k_j for j <= t ----
-      if (!group_wait(sm, B_GATES + s, (i >> 1) & 1, 2, 128, pleader)) break;
+      if (!group_wait(sm, B_REC_FULL + s, (i >> 1) & 1, 2, 128, pleader)) break;
       if (!group_wait(sm, B_KKQK, i & 1, 2, 128, pleader)) break;
       tc::fence_after_sync();
       // P rows from Q K^T (D1 columns 64-127; every lane quarter holds the 64 Q rows):
@@ -552,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_before_sync();
       named_sync(2, 128);
       if (pleader) {
-        mbar_arrive(sm.bar(B_P_READY));
+        mbar_arrive(sm.bar(B_D_READY));  // P tile written, S0 Q^T scaled
         mbar_arrive(sm.bar(B_GFREE + s));
       }
     }
@@ -599,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nchunks; ++i) {
       const int s = i & 1;
       const uint32_t d1 = kTmD1 + (uint32_t)s * 128;
-      if (!group_wait(sm, B_GATES + s, (i >> 1) & 1, 1, kChainThreads, leader)) break;
+      if (!group_wait(sm, B_REC_FULL + s, (i >> 1) & 1, 1, kChainThreads, leader)) break;
       const float GC = sm.gate(s, GA_G)[63];
       // ---- S0 hi/lo into TMEM (A of the first MMA): the thread's 32 state columns in one
       //      load, kept in registers for the G_C scaling below ----
