@@ -524,8 +524,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         emit_out(i - 1);
       }
-      // ---- S0 Q^T of chunk i scaled by G (column t by G_t), once the chain has read R's
-      //      inputs (the first MMA is done; its TMEM traffic is over) ----
+      // ---- S0 Q^T of chunk i scaled by G (column t by G_t), and the state S <- G_C S (this
+      //      thread's row), once the chain has read R's inputs (the first MMA is done and the
+      //      chain's S0 split has read S); the state MMA waits for this (its barrier counts the
+      //      P warpgroup) ----
       if (!group_wait(sm, B_R_READY, i & 1, 2, 128, pleader)) break;
       tc::fence_after_sync();
       {
@@ -546,12 +548,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc::tmem_st16(ta, x);
         }
+        const float GC = sm.gate(s, GA_G)[63];
+#pragma unroll 1
+        for (int c16 = 0; c16 < 8; ++c16) {
+          float x[16];
+          const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + c16 * 16);
+          tc::tmem_ld16(ta, x);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 16; ++u) x[u] *= GC;
+          tc::tmem_st16(ta, x);
+        }
         tc::tmem_wait_st();
       }
       tc::fence_before_sync();
       named_sync(2, 128);
       if (pleader) {
-        mbar_arrive(sm.bar(B_D_READY));  // P tile written, S0 Q^T scaled
+        mbar_arrive(sm.bar(B_D_READY));  // P tile written, S0 Q^T and S scaled
         mbar_arrive(sm.bar(B_GFREE + s));
       }
     }
@@ -599,7 +612,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = i & 1;
       const uint32_t d1 = kTmD1 + (uint32_t)s * 128;
       if (!group_wait(sm, B_REC_FULL + s, (i >> 1) & 1, 1, kChainThreads, leader)) break;
-      const float GC = sm.gate(s, GA_G)[63];
       // ---- S0 hi/lo into TMEM (A of the first MMA): the thread's 32 state columns in one
       //      load, kept in registers for the G_C scaling below ----
       if (i > 0 && !group_wait(sm, B_MMA4 + ((i - 1) & 1), ((i - 1) >> 1) & 1, 1, kChainThreads, leader)) break;
@@ -619,35 +631,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_before_sync();
       named_sync(1, kChainThreads);
       if (leader) mbar_arrive(sm.bar(B_S0_READY));
-      // ---- S <- G_C * S while the first MMA runs (it reads only the hi/lo copies; the
-      //      state MMA of this chunk comes after the deltas) ----
-#pragma unroll
-      for (int q = 0; q < kStateCols; ++q) xs[q] *= GC;
-      tc::tmem_st32(tc::tmem_addr(tmem, lane_base, kTmS + sc), xs);
-      tc::tmem_wait_st();
+      // (S <- G_C S is done by the P warpgroup once R is ready, before the state MMA)
       // ---- while the first MMA runs: beta_t V[t][v] and beta_t G_t of this thread's 16 token
-      //      columns, and the state-update decays exp(g_C - g_t), into registers ----
+      //      columns into registers ----
       static_assert(kTokCols == 16, "one 16-token piece per chain thread");
       if (!group_wait(sm, B_V_FULL, i & 1, 1, kChainThreads, leader)) break;
-      float bv[16], bgx[16], rdec[16];
+      float bv[16], bgx[16];
       {
         const float* bet = sm.gate(s, GA_BETA) + tb;
         const float* bg = sm.gate(s, GA_BG) + tb;
-        const float* rr = sm.gate(s, GA_R) + tb;
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
           const float4 b4 = *reinterpret_cast<const float4*>(bet + 4 * u4);
           const float4 g4 = *reinterpret_cast<const float4*>(bg + 4 * u4);
-          const float4 r4 = *reinterpret_cast<const float4*>(rr + 4 * u4);
           const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, gg[4] = {g4.x, g4.y, g4.z, g4.w};
-          const float rq[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int u = 4 * u4 + e;
             // a state map's homogeneous part takes v as 0
             bv[u] = homog ? 0.f : bb[e] * __bfloat162float(vt[(tb + u) * kHeadDim + v]);
             bgx[u] = gg[e];
-            rdec[u] = rq[e];
           }
         }
       }
@@ -674,7 +677,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(sm.bar(B_V_EMPTY));
       }
       // ---- deltas: Dt^T = D^T exp(gC - g) (hi/lo into TMEM, state MMA) first; then D^T as a
-      //      bf16 tile for the output MMA, after the state MMA has been released ----
+      //      bf16 tile for the output MMA, after the state MMA has been released.  The decays
+      //      exp(g_C - g_t) are loaded while MMA2 runs. ----
+      float rdec[16];
+      {
+        const float* rr = sm.gate(s, GA_R) + tb;
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const float4 r4 = *reinterpret_cast<const float4*>(rr + 4 * u4);
+          rdec[4 * u4] = r4.x;
+          rdec[4 * u4 + 1] = r4.y;
+          rdec[4 * u4 + 2] = r4.z;
+          rdec[4 * u4 + 3] = r4.w;
+        }
+      }
       if (!group_wait(sm, B_MMA2, i & 1, 1, kChainThreads, leader)) break;
       tc::fence_after_sync();
       float d[16];
