@@ -102,7 +102,8 @@ static_assert(kSmAlloc <= 232448, "smem budget");
 enum : int {
   B_KQ_FULL = 0,    // [2]
   B_KQ_EMPTY = 2,   // [2]
-  B_REC_FULL = 4,   // [2] record landed: T (hi | lo) and the gate arrays (one expect_tx, two copies)
+  B_REC_FULL = 4,   // [2] chunk inputs landed: T (hi | lo), the gate arrays and V (one expect_tx,
+                    //     three copies)
   B_GFREE = 6,      // [2] chain and P warpgroup are done with a gate stage (2 arrivals)
   B_T_UNUSED = 8,   // [2] (unused)
   B_T_EMPTY = 10,   // [2] the MMA reading a T stage has completed
@@ -110,7 +111,7 @@ enum : int {
   B_MMA4 = 14,      // [2] state update of a chunk done (per chunk parity)
   B_KKQK = 16,      // [K; Q] K^T of a chunk is in its D1 buffer, columns 0-63
   B_D0_UNUSED,      // (unused)
-  B_V_FULL,
+  B_V_UNUSED,       // (unused)
   B_V_EMPTY,
   B_S0_READY,       // MMA1 may go: S0 hi/lo written (chain) and the P warpgroup has read the Q K^T
                     // of the chunk's D1 buffer (having stored the outputs of chunk i - 2 from it)
@@ -292,9 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int z = (int)(t0 + (int64_t)i * kC);
         const unsigned char* rec = record(p, slot0 + i, h);
         // waits in the order their phases complete: MMA2(i-2), deltas(i-2), MMA4(i-2), R(i-1).
-        // One barrier counts both parts of the record (its phase completes once both landed).
+        // One barrier counts the record's two parts and V (its phase completes once all landed;
+        // V, the last, is issued once R of chunk i - 1 has read the previous V).
         if (i >= 2 && !wait_bar(sm, sm.bar(B_T_EMPTY + s), ph)) break;
-        mbar_arrive_expect_tx(sm.bar(B_REC_FULL + s), kRecBytes);
+        mbar_arrive_expect_tx(sm.bar(B_REC_FULL + s), kRecBytes + 16384);
         bulk_g2s(sm.base + kSmT + s * kTStage, rec, kRecT, sm.bar(B_REC_FULL + s));
         if (i >= 2 && !wait_bar(sm, sm.bar(B_GFREE + s), ph)) break;
         bulk_g2s(sm.base + kSmGate + s * kRecGates, rec + kRecT, kRecGates, sm.bar(B_REC_FULL + s));
@@ -309,8 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::tma_load_3d(kq + f * kKQTile + kRowsK, &mapK, 64 * f, qh, z, full);
         }
         if (i >= 1 && !wait_bar(sm, sm.bar(B_V_EMPTY), (i - 1) & 1)) break;
-        mbar_arrive_expect_tx(sm.bar(B_V_FULL), 16384);
-        tc::tma_load_3d(sm.base + kSmV, &mapV, 0, h, z, sm.bar(B_V_FULL));
+        tc::tma_load_3d(sm.base + kSmV, &mapV, 0, h, z, sm.bar(B_REC_FULL + s));
         issued = i + 1;
       }
       // drain: the last loads have landed before the CTA can exit (bounded)
@@ -318,7 +319,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = issued - 1, s = i & 1;
         wait_bar(sm, sm.bar(B_REC_FULL + s), (i >> 1) & 1);
         wait_bar(sm, sm.bar(B_KQ_FULL + s), (i >> 1) & 1);
-        wait_bar(sm, sm.bar(B_V_FULL), i & 1);
       }
     }
   }
@@ -524,10 +524,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         emit_out(i - 1);
       }
-      // ---- S0 Q^T of chunk i scaled by G (column t by G_t), and the state S <- G_C S (this
-      //      thread's row), once the chain has read R's inputs (the first MMA is done and the
-      //      chain's S0 split has read S); the state MMA waits for this (its barrier counts the
-      //      P warpgroup) ----
+      // ---- S0 Q^T of chunk i scaled by G (column t by G_t), once the chain has read R's
+      //      inputs (the first MMA is done; its TMEM traffic is over) ----
       if (!group_wait(sm, B_R_READY, i & 1, 2, 128, pleader)) break;
       tc::fence_after_sync();
       {
@@ -548,23 +546,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc::tmem_st16(ta, x);
         }
-        const float GC = sm.gate(s, GA_G)[63];
-#pragma unroll 1
-        for (int c16 = 0; c16 < 8; ++c16) {
-          float x[16];
-          const uint32_t ta = tc::tmem_addr(tmem, lane_base, kTmS + c16 * 16);
-          tc::tmem_ld16(ta, x);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int u = 0; u < 16; ++u) x[u] *= GC;
-          tc::tmem_st16(ta, x);
-        }
         tc::tmem_wait_st();
       }
       tc::fence_before_sync();
       named_sync(2, 128);
       if (pleader) {
-        mbar_arrive(sm.bar(B_D_READY));  // P tile written, S0 Q^T and S scaled
+        mbar_arrive(sm.bar(B_D_READY));  // P tile written, S0 Q^T scaled
         mbar_arrive(sm.bar(B_GFREE + s));
       }
     }
@@ -631,11 +618,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_before_sync();
       named_sync(1, kChainThreads);
       if (leader) mbar_arrive(sm.bar(B_S0_READY));
-      // (S <- G_C S is done by the P warpgroup once R is ready, before the state MMA)
+      // ---- S <- G_C * S while the first MMA runs (it reads only the hi/lo copies; the
+      //      state MMA of this chunk comes after the deltas) ----
+      {
+        const float GC = sm.gate(s, GA_G)[63];
+#pragma unroll
+        for (int q = 0; q < kStateCols; ++q) xs[q] *= GC;
+        tc::tmem_st32(tc::tmem_addr(tmem, lane_base, kTmS + sc), xs);
+        tc::tmem_wait_st();
+      }
       // ---- while the first MMA runs: beta_t V[t][v] and beta_t G_t of this thread's 16 token
       //      columns into registers ----
       static_assert(kTokCols == 16, "one 16-token piece per chain thread");
-      if (!group_wait(sm, B_V_FULL, i & 1, 1, kChainThreads, leader)) break;
       float bv[16], bgx[16];
       {
         const float* bet = sm.gate(s, GA_BETA) + tb;
