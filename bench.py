@@ -215,31 +215,43 @@ def set_bytes(s):
     return sum(v.numel() * v.element_size() for v in s.values() if torch.is_tensor(v))
 
 
-def time_steps(call, sets, steps, warmup, world, sampler=None):
+def time_steps(call, sets, steps, warmup, world, sampler=None, graph=False):
     """Warm up, then time exactly ``steps`` calls bracketed by barrier +
-    synchronize; per-launch CUDA events on the launching stream give the
-    kernel's average duration.  Returns (ms_per_step max over ranks, avg launch ms)."""
+    synchronize, with CUDA events on the launching stream around the timed region
+    only (events recorded between the steps would add their own gaps to it).
+    With ``graph`` the ``steps`` calls are captured once into a CUDA graph (the
+    serving form of a decode loop) and the timed region is one replay of it; the
+    first replay, untimed, uploads the graph.  Returns (ms per step, max over
+    ranks; this rank's ms per step = the average duration of one step's launches)."""
     stream = torch.cuda.current_stream()
     for i in range(warmup):
         call(sets[i % len(sets)])
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    g = None
+    if graph:
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                call(sets[i % len(sets)])
+        g.replay()
+        torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     ctx = sampler if sampler is not None else _Null()
     with ctx:
         t0.record(stream)
-        for i in range(steps):
-            starts[i].record(stream)
-            call(sets[i % len(sets)])
-            ends[i].record(stream)
+        if g is not None:
+            g.replay()
+        else:
+            for i in range(steps):
+                call(sets[i % len(sets)])
         t1.record(stream)
         torch.cuda.synchronize()
     barrier(world)
     total_ms = t0.elapsed_time(t1)
-    launch_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
-    return max_over_ranks(total_ms, world) / steps, launch_ms
+    del g
+    return max_over_ranks(total_ms, world) / steps, total_ms / steps
 
 
 class _Null:
@@ -423,7 +435,8 @@ def run_ours(args, world, rank, local):
         n_sets = max(2, math.ceil(3 * L2_BYTES / set_bytes(one[0])))
         sets = one + decode_sets(gdn, batch, n_sets - 1, seed=rank + 1, device="cuda")
         sampler = ClockSampler(local)
-        ms, launch_ms = time_steps(lambda s: decode_call(gdn, s), sets, args.steps, args.warmup, world, sampler)
+        ms, launch_ms = time_steps(lambda s: decode_call(gdn, s), sets, args.steps, args.warmup, world, sampler,
+                                   graph=True)
         bytes_rank = gdn.workloads.decode_bytes_per_seq() * batch
         total_bytes = sum_over_ranks(bytes_rank, world)
         value = total_bytes / (ms * 1e-3) / 1e9
@@ -436,7 +449,9 @@ def run_ours(args, world, rank, local):
                     "head_dim": 128, "state": "fp32 k-last", "rotating_buffer_sets": len(sets),
                     "l2": f"inputs larger than L2: {len(sets)} rotating sets, "
                           f"{len(sets) * set_bytes(sets[0]) / 1e6:.0f} MB footprint",
-                    "parallelism": f"dp{world} (sequences sharded, no collective)"},
+                    "parallelism": f"dp{world} (sequences sharded, no collective)",
+                    "timing": "the K steps replayed from one CUDA graph (the serving form of a decode loop); "
+                              "CUDA events around the timed region only"},
             roofline={"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                       "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)",
                       "traffic": profile_traffic("gdn_decode_b64"),
@@ -455,7 +470,7 @@ def run_ours(args, world, rank, local):
         msteps = args.steps if wl == "mtp_b64_t4" else max(20, min(200, args.steps // 10))
         mwarm = args.warmup if wl == "mtp_b64_t4" else 5
         sampler_m = ClockSampler(local) if wl == "mtp_b64_t4" else None
-        mms, mlaunch = time_steps(lambda s: mtp_call(gdn, s), msets, msteps, mwarm, world, sampler_m)
+        mms, mlaunch = time_steps(lambda s: mtp_call(gdn, s), msets, msteps, mwarm, world, sampler_m, graph=True)
         mbytes = gdn.workloads.mtp_bytes_per_seq(mt) * mb
         mres = {"workload": "mtp_b64_t4", "gbs": sum_over_ranks(mbytes, world) / (mms * 1e-3) / 1e9,
                 "tokens_per_s": sum_over_ranks(mb * mt, world) / (mms * 1e-3), "ms_per_step": mms,
@@ -544,7 +559,7 @@ def run_ours(args, world, rank, local):
             result.update(metric="GDN prefill tokens/s", value=pres["tokens_per_s"], unit="tokens/s",
                           ms_per_step=pms, dtype="bf16", config={"workload": wl_p, "seqlens_per_rank": seqlens,
                                                                  "parallelism": f"dp{world}"},
-                          roofline=pres["roofline"], gpu_launches=psteps, clocks=sampler_p.summary(),
+                          roofline=pres["roofline"], gpu_launches=2 * psteps, clocks=sampler_p.summary(),
                           e2e=None)
         else:
             result["prefill"] = pres
