@@ -264,29 +264,61 @@ class _Null:
 
 # ----------------------------------------------------------------------------- e2e
 def decode_e2e(gdn, batch, steps, warmup, world, seed):
-    """Public API with host buffers: pinned host inputs -> device, run(), outputs -> pinned host."""
+    """Public API with host buffers: every step copies its inputs (the state
+    included) from pinned host memory to the device, runs the decode
+    (``kernel_decode.run_dps``) and copies the output and the new state back to
+    pinned host memory.  Copies in, compute and copies out run on three streams
+    over two device buffer sets, so step i's inputs go up while step i - 1's
+    results come down (the two PCIe directions overlap, as in a serving loop)."""
     host = gdn.workloads.decode_inputs(batch, seed=seed)
-    pinned = {k: (v.pin_memory() if torch.is_tensor(v) else v) for k, v in host.items()}
+    names = [k for k, v in host.items() if torch.is_tensor(v)]
+    pinned = {k: host[k].pin_memory() for k in names}
+    scale = host["scale"]
     out_h = torch.empty(batch, 1, 32, 128, dtype=torch.bfloat16).pin_memory()
     st_h = torch.empty(batch, 32, 128, 128, dtype=torch.float32).pin_memory()
-    h2d = sum(v.numel() * v.element_size() for v in pinned.values() if torch.is_tensor(v))
+    dev = [{k: torch.empty_like(pinned[k], device="cuda") for k in names} for _ in range(2)]
+    outs = [(torch.empty(batch, 1, 32, 128, dtype=torch.bfloat16, device="cuda"),
+             torch.empty(batch, 32, 128, 128, dtype=torch.float32, device="cuda")) for _ in range(2)]
+    s_comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # inputs of buffer set b are on the device
+    ev_comp = [torch.cuda.Event() for _ in range(2)]  # the decode on set b is done (inputs read)
+    ev_out = [torch.cuda.Event() for _ in range(2)]   # the results of set b are back on the host
+    used = [False, False]
+    h2d = sum(pinned[k].numel() * pinned[k].element_size() for k in names)
     d2h = out_h.numel() * 2 + st_h.numel() * 4
 
-    def step():
-        d = {k: (v.to("cuda", non_blocking=True) if torch.is_tensor(v) else v) for k, v in pinned.items()}
-        o, ns = gdn.kernel_decode.run(**d)
-        out_h.copy_(o, non_blocking=True)
-        st_h.copy_(ns, non_blocking=True)
+    def step(i):
+        b = i % 2
+        d = dev[b]
+        if used[b]:
+            s_in.wait_event(ev_comp[b])
+        with torch.cuda.stream(s_in):
+            for k in names:
+                d[k].copy_(pinned[k], non_blocking=True)
+        ev_in[b].record(s_in)
+        s_comp.wait_event(ev_in[b])
+        if used[b]:
+            s_comp.wait_event(ev_out[b])
+        gdn.kernel_decode.run_dps(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
+                                  scale, outs[b][0], outs[b][1])
+        ev_comp[b].record(s_comp)
+        s_out.wait_event(ev_comp[b])
+        with torch.cuda.stream(s_out):
+            out_h.copy_(outs[b][0], non_blocking=True)
+            st_h.copy_(outs[b][1], non_blocking=True)
+        ev_out[b].record(s_out)
+        used[b] = True
 
-    for _ in range(warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
-    t0.record()
-    for _ in range(steps):
-        step()
-    t1.record()
+    t0.record(s_in)
+    for i in range(steps):
+        step(warmup + i)
+    t1.record(s_out)
     torch.cuda.synchronize()
     barrier(world)
     return max_over_ranks(t0.elapsed_time(t1), world) / steps, h2d, d2h
@@ -459,7 +491,7 @@ def run_ours(args, world, rank, local):
                       "algorithmic_bytes_per_launch": bytes_rank},
             e2e={"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                  "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                 "path": "kernel_decode.run() with pinned host inputs/outputs (state in and out)"},
+                 "path": "kernel_decode.run_dps() with pinned host inputs and outputs (state in and out every step); copies in, decode and copies out on three streams over two device buffer sets"},
             gpu_launches=args.steps,
             clocks=sampler.summary())
         del sets
