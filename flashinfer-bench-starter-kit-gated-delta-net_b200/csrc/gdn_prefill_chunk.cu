@@ -264,6 +264,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nchunks = ce - cb;
   const int64_t slot0 = slot_start(cu0, n) + cb;  // workspace record slot of the range's chunk 0
 
+  // chain threads: their 32 columns of the initial state (row (warp % 4) * 32 + lane, columns
+  // (warp / 4) * 32 ..), loaded before the setup below so the memory round trip overlaps it
+  float st_init[kStateCols];
+  if (warp < kChainWarps) {
+    const float* init_blk = init_block();
+    const float* src =
+        init_blk ? init_blk + (size_t)((warp & 3) * 32 + lane) * kHeadDim + (warp >> 2) * kStateCols : nullptr;
+#pragma unroll
+    for (int q = 0; q < kStateCols; q += 4) {
+      const float4 f = src ? ld_nc_f4(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      st_init[q] = f.x;
+      st_init[q + 1] = f.y;
+      st_init[q + 2] = f.z;
+      st_init[q + 3] = f.w;
+    }
+  }
+
   if (tid == 0) {
     for (int i = 0; i < B_COUNT; ++i)
       mbar_init(sm.bar(i), (i == B_GFREE || i == B_GFREE + 1 || i == B_S0_READY || i == B_D_READY) ? 2 : 1);
@@ -570,27 +587,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = tid == 0;
     const int sc = hsel * kStateCols;  // this thread's state columns [sc, sc + kStateCols)
     const int tb = hsel * kTokCols;    // this thread's token columns [tb, tb + kTokCols)
-    // initial state (this thread's columns) -> TMEM S: loaded, zero or the identity
+    // initial state (this thread's columns, loaded above) -> TMEM S: loaded, zero or the identity
     {
-      const float* init_blk = init_block();
-      const float* src = init_blk ? init_blk + (size_t)v * kHeadDim + sc : nullptr;
+      if (homog) {
 #pragma unroll
-      for (int c0 = 0; c0 < kStateCols; c0 += 16) {
-        float x[16];
-#pragma unroll
-        for (int q = 0; q < 16; q += 4) {
-          const float4 f = src ? ld_nc_f4(src + c0 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-          x[q] = f.x;
-          x[q + 1] = f.y;
-          x[q + 2] = f.z;
-          x[q + 3] = f.w;
-        }
-        if (homog) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) x[q] = (sc + c0 + q == v) ? 1.f : 0.f;
-        }
-        tc::tmem_st16(tc::tmem_addr(tmem, lane_base, kTmS + sc + c0), x);
+        for (int q = 0; q < kStateCols; ++q) st_init[q] = (sc + q == v) ? 1.f : 0.f;
       }
+      tc::tmem_st32(tc::tmem_addr(tmem, lane_base, kTmS + sc), st_init);
       tc::tmem_wait_st();
     }
     unsigned char* dtile = sm.base + kSmD;
