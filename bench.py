@@ -182,6 +182,21 @@ def prefill_sets(gdn, seqlens, n_sets, seed, device, zero_state=False):
     return sets
 
 
+def prefill_launches(gdn, seqlens):
+    """Kernels one prefill step launches: prep + chain, or with the automatic in-GPU
+    segments prep + pass 1 (+ the map composition for 3 or more segments) + reruns.
+    The segment count is read off the workspace size, whose extra part is one fp32
+    state per (sequence, v-head) for 2 segments and 3 S - 5 of them for S >= 3."""
+    N, T = len(seqlens), sum(seqlens)
+    auto = gdn.kernel_prefill.workspace_size(N, T, 16, 32)
+    one = gdn.kernel_prefill.workspace_size(N, T, 16, 32, segments=1)
+    if auto <= one:
+        return 2
+    per_state = N * 32 * 128 * 128 * 4
+    segs = round(((auto - one) // per_state + 5) / 3) if (auto - one) >= 2 * per_state else 2
+    return 4 if segs >= 3 else 3
+
+
 def prefill_call(gdn, s):
     gdn.kernel_prefill.run_dps(s["q"], s["k"], s["v"], s["state"], s["A_log"], s["a"], s["dt_bias"],
                                s["b"], s["cu_seqlens"], s["scale"], s["output"], s["new_state"])
@@ -591,8 +606,12 @@ def run_ours(args, world, rank, local):
             result.update(metric="GDN prefill tokens/s", value=pres["tokens_per_s"], unit="tokens/s",
                           ms_per_step=pms, dtype="bf16", config={"workload": wl_p, "seqlens_per_rank": seqlens,
                                                                  "parallelism": f"dp{world}"},
-                          roofline=pres["roofline"], gpu_launches=2 * psteps, clocks=sampler_p.summary(),
+                          roofline=pres["roofline"], gpu_launches=prefill_launches(gdn, seqlens) * psteps,
+                          clocks=sampler_p.summary(),
                           e2e=None)
+            if wl_p == "prefill_8x32768":
+                # configs[4] is one fixed batch of 8 sequences split over the ranks (strong scaling)
+                result["scaling"] = "strong"
         else:
             result["prefill"] = pres
         del psets
