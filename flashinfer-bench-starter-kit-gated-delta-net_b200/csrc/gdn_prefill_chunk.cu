@@ -24,22 +24,28 @@
 // precomputed from the prep kernel (gdn_prefill_prep.cu) as one workspace record
 // per (chunk slot, v-head), bulk-copied into shared memory one chunk ahead.
 //
-// CTA = one (sequence, v-head) chain, 4 kCW + 6 warps:
+// CTA = one (sequence, v-head) chain (sequences started longest first), 4 kCW + 6 warps:
 //   4 kCW chain warps: thread (warp & 3, lane) owns state row v, warp >> 2
-//               selects 1/kCW of the columns; S0 hi/lo and G_C scaling, R,
-//               deltas, initial/final state I/O
-//   4 P warps   P from Q K^T one chunk ahead (Q rows on all 128 TMEM lanes),
-//               G-scaling of S0 Q^T in TMEM, the outputs of the previous chunk
-//               (TMEM -> bf16 rows in shared memory -> one TMA store)
-//   1 TMA warp  T and gate records (bulk), K, Q (128B-swizzled tiles), V
-//               (plain); all double-buffered except V
+//               selects 1/kCW of the columns; initial state (loaded before the
+//               CTA setup), S0 hi/lo and G_C scaling, R, deltas, the D^T tile,
+//               final state
+//   4 P warps   P from Q K^T (Q rows on all 128 TMEM lanes), G-scaling of S0 Q^T
+//               in TMEM, the outputs of the previous chunk (TMEM -> bf16 rows in
+//               shared memory -> one TMA store)
+//   1 TMA warp  record (T tiles + gates) by bulk copy, K, Q (128B-swizzled tiles),
+//               V (plain); all double-buffered except V
 //   1 MMA warp  TMEM allocator and MMA issuer
-// Per chunk the state chain is S0 hi/lo -> [S0 [K;Q]^T] -> R -> [R^T T^T] ->
-// deltas -> [S += Dt^T K] -> next chunk; Q K^T, the output MMA (D^T P^T), the
-// output stores and the P work overlap it.  Hand-offs are mbarriers; every wait is
-// bounded (kWaitLimitNs): a timeout raises GDN_DEVERR_WAIT_TIMEOUT and an
-// in-CTA abort flag so every role leaves its loop, then in-flight copies and
-// MMAs are drained before TMEM is freed.
+// Per chunk the state chain is S0 hi/lo -> [S0 [Q;K]^T] -> R -> [R^T T^T] ->
+// deltas -> [S += Dt^T K] -> next chunk; the next chunk's Q K^T (in two halves, in
+// the tensor pipe's idle windows), the output MMA (D^T P^T), the output stores and
+// the P work overlap it.  Hand-offs are mbarriers, arranged so the MMA thread waits
+// on one barrier per MMA group (a barrier probe costs it several hundred cycles even
+// after the phase completed; a wait that blocks first wakes quickly): MMA1 waits on
+// the chain's S0 split and the P warps' read of Q K^T together, MMA4 and the output
+// MMA on the deltas and the P tile together, and one barrier completes when a chunk's
+// record, gates and V have landed.  Every wait is bounded (kWaitLimitNs): a timeout
+// raises GDN_DEVERR_WAIT_TIMEOUT and an in-CTA abort flag so every role leaves its
+// loop, then in-flight copies and MMAs are drained before TMEM is freed.
 #include <cuda.h>
 
 #include "gdn_prefill_chunk.cuh"
