@@ -111,13 +111,9 @@ enum : int {
   B_REC_FULL = 4,   // [2] chunk inputs landed: T (hi | lo), the gate arrays and V (one expect_tx,
                     //     three copies)
   B_GFREE = 6,      // [2] chain and P warpgroup are done with a gate stage (2 arrivals)
-  B_T_UNUSED = 8,   // [2] (unused)
-  B_T_EMPTY = 10,   // [2] the MMA reading a T stage has completed
-  B_OUT_UNUSED = 12,  // [2] (unused)
-  B_MMA4 = 14,      // [2] state update of a chunk done (per chunk parity)
-  B_KKQK = 16,      // [K; Q] K^T of a chunk is in its D1 buffer, columns 0-63
-  B_D0_UNUSED,      // (unused)
-  B_V_UNUSED,       // (unused)
+  B_T_EMPTY = 8,    // [2] the MMA reading a T stage has completed
+  B_MMA4 = 10,      // [2] state update of a chunk done (per chunk parity)
+  B_KKQK = 12,      // [Q; Q] K^T of a chunk is in its D1 buffer, columns 64-127
   B_V_EMPTY,
   B_S0_READY,       // MMA1 may go: S0 hi/lo written (chain) and the P warpgroup has read the Q K^T
                     // of the chunk's D1 buffer (having stored the outputs of chunk i - 2 from it)
@@ -127,7 +123,6 @@ enum : int {
   B_D_READY,        // MMA4 may go: Dt hi/lo written (chain), and the P warpgroup has written the
                     // P tile and scaled S0 Q^T (so the output MMA after MMA4 needs only the D^T tile)
   B_MMA3,
-  B_P_UNUSED,       // (unused)
   B_DTILE,          // D^T bf16 tile written (A of the output MMA)
   B_DRAIN,
   B_COUNT
