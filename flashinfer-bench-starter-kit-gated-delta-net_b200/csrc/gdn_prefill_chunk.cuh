@@ -94,7 +94,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 // (a, b) -> bf16x2 hi and bf16x2 lo with a = hi + lo to ~16 mantissa bits.
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
   hi = pack_bf16x2(a, b);
-  lo = pack_bf16x2(a - __uint_as_float(hi << 16), b - __uint_as_float(hi & 0xffff0000u));
+  // both residuals (a, b) - hi in one packed fp32x2 FMA (exact: hi is a's / b's leading bits)
+  const float2 r = __ffma2_rn(make_float2(__uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u)),
+                              make_float2(-1.f, -1.f), make_float2(a, b));
+  lo = pack_bf16x2(r.x, r.y);
 }
 
 // 16-byte store of 8 bf16 (columns 8*c8 .. 8*c8+7 of `row`) into a SW128 tile.
