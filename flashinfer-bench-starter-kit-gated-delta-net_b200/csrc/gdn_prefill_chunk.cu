@@ -627,7 +627,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         const float GC = sm.gate(s, GA_G)[63];
 #pragma unroll
-        for (int q = 0; q < kStateCols; ++q) xs[q] *= GC;
+        for (int q = 0; q < kStateCols; q += 2) {
+          const float2 y = __fmul2_rn(make_float2(xs[q], xs[q + 1]), make_float2(GC, GC));
+          xs[q] = y.x;
+          xs[q + 1] = y.y;
+        }
         tc::tmem_st32(tc::tmem_addr(tmem, lane_base, kTmS + sc), xs);
         tc::tmem_wait_st();
       }
@@ -648,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int u = 4 * u4 + e;
             // a state map's homogeneous part takes v as 0
             bv[u] = homog ? 0.f : bb[e] * __bfloat162float(vt[(tb + u) * kHeadDim + v]);
-            bgx[u] = gg[e];
+            bgx[u] = -gg[e];  // negated: R = beta V - beta G x as one FMA
           }
         }
       }
@@ -661,9 +665,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_wait_ld();
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
-          split2(fmaf(-bgx[2 * u], x[2 * u], bv[2 * u]), fmaf(-bgx[2 * u + 1], x[2 * u + 1], bv[2 * u + 1]), hi[u],
-                 lo[u]);
+        for (int u = 0; u < 8; ++u) {
+          const float2 r = __ffma2_rn(make_float2(bgx[2 * u], bgx[2 * u + 1]), make_float2(x[2 * u], x[2 * u + 1]),
+                                      make_float2(bv[2 * u], bv[2 * u + 1]));
+          split2(r.x, r.y, hi[u], lo[u]);
+        }
         tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRhi + tb / 2), hi);
         tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmRlo + tb / 2), lo);
       }
@@ -697,7 +703,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tmem_wait_ld();
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) split2(d[2 * u] * rdec[2 * u], d[2 * u + 1] * rdec[2 * u + 1], hi[u], lo[u]);
+        for (int u = 0; u < 8; ++u) {
+          const float2 e = __fmul2_rn(make_float2(d[2 * u], d[2 * u + 1]), make_float2(rdec[2 * u], rdec[2 * u + 1]));
+          split2(e.x, e.y, hi[u], lo[u]);
+        }
         tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDthi + tb / 2), hi);
         tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, kTmDtlo + tb / 2), lo);
       }
