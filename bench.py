@@ -10,9 +10,19 @@ each rank owns its own 64 sequences and states (weak scaling, no collective),
 one decode call over the batch; inputs are resident in HBM and rotate over
 several buffer sets whose footprint exceeds 3x L2 (126 MB), so no step reads
 L2-resident state.  ``e2e`` times the public ``run()`` with host (pinned)
-inputs and outputs, copies included.  ``prefill`` reports configs[3] (varlen,
-16 sequences) tokens/s on the same ranks, ``mtp`` the pooled multi-token decode
-(64 sequences x 4 tokens, in-place state pool) GB/s against the HBM roofline.
+inputs and outputs, copies included.
+
+Further legs of the same line (each with its own CUDA-event timing, roofline and
+clock record): ``decode_b1024`` = configs[2] (1024 sequences split over the N
+ranks, strong scaling), ``prefill`` = configs[3] (varlen, 16 sequences, on every
+rank), ``prefill_8x32768`` = configs[4] (8 x 32768 tokens split over the ranks by
+sequence, strong scaling), ``mtp`` = pooled multi-token decode (64 sequences x 4
+tokens, in-place state pool).  At N = 1 rank 0 also times the CPU baselines (the
+C restatement of the reference recurrence for decode and prefill, and the
+flashinfer torch reference recurrence) and ``reference_triton``: the reference's
+own Triton kernels (``solution/triton/kernel_{decode,prefill}.py::run``,
+unmodified, staged in ``baseline/_ref``) on this GPU beside this library, on
+configs[1], configs[3] and the reference's own qk4/v8 shapes.
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 C restatement in ``oracle/``, all host threads) on a bounded sample of the
@@ -21,6 +31,7 @@ same workload and prints the same line with ``"impl": "reference"``.
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import math
 import os
@@ -416,6 +427,236 @@ def cpu_mtp_rate(gdn, batch, tokens, budget_s, nthreads=None):
     return gb / el, f"{reps} calls of B={batch} x T={tokens} tokens (16/32 heads) in {el:.1f} s", cores
 
 
+# ----------------------------------------------------------------------------- legs
+def leg_steps(steps: int, cap: int, floor: int = 10) -> int:
+    """Timed steps of a secondary leg: the run's K, capped so the default run stays short."""
+    return max(floor, min(steps, cap))
+
+
+def decode_leg(gdn, wl, world, rank, local, steps, warmup, peaks, with_e2e):
+    """configs[1] (``decode_b64``: 64 sequences per rank, weak scaling) or configs[2]
+    (``decode_b1024``: 1024 sequences split over the ranks, strong scaling)."""
+    hbm_peak, _, _, peak_kind = peaks
+    if wl == "decode_b64":
+        batch = 64
+    else:
+        lo, hi = gdn.sharding.batch_slice(1024, world, rank)
+        batch = hi - lo
+    one = decode_sets(gdn, batch, 1, seed=rank, device="cuda")
+    n_sets = max(2, math.ceil(3 * L2_BYTES / set_bytes(one[0])))
+    sets = one + decode_sets(gdn, batch, n_sets - 1, seed=rank + 1, device="cuda")
+    sampler = ClockSampler(local)
+    ms, launch_ms = time_steps(lambda s: decode_call(gdn, s), sets, steps, warmup, world, sampler, graph=True)
+    bytes_rank = gdn.workloads.decode_bytes_per_seq() * batch
+    total_bytes = sum_over_ranks(bytes_rank, world)
+    achieved = bytes_rank / (launch_ms * 1e-3) / 1e9
+    res = dict(
+        workload=wl, gbs=total_bytes / (ms * 1e-3) / 1e9,
+        tokens_per_s=sum_over_ranks(batch, world) / (ms * 1e-3), ms_per_step=ms, steps=steps,
+        batch_per_rank=batch, rotating_buffer_sets=len(sets),
+        l2=f"inputs larger than L2: {len(sets)} rotating sets, {len(sets) * set_bytes(sets[0]) / 1e6:.0f} MB footprint",
+        scaling="weak" if wl == "decode_b64" else "strong",
+        roofline={"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                  "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)",
+                  "traffic": profile_traffic(f"gdn_{wl}"), "kernel": "decode_kernel",
+                  "avg_launch_us": launch_ms * 1e3, "algorithmic_bytes_per_launch": bytes_rank},
+        clocks=sampler.summary())
+    del sets
+    if with_e2e:
+        e2e_steps = leg_steps(steps, 50, floor=20)
+        e2e_ms, h2d, d2h = decode_e2e(gdn, batch, e2e_steps, 3, world, seed=rank)
+        res["e2e"] = {"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                      "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "steps": e2e_steps,
+                      "path": "kernel_decode.run_dps() with pinned host inputs and outputs (state in and out "
+                              "every step); copies in, decode and copies out on three streams over two device "
+                              "buffer sets"}
+    torch.cuda.empty_cache()
+    return res
+
+
+def prefill_leg(gdn, wl_p, world, rank, local, steps, warmup, peaks):
+    """configs[3] (``prefill_varlen16``, the whole batch on every rank) or configs[4]
+    (``prefill_8x32768``, sequences split over the ranks: strong scaling)."""
+    _, bf16_peak, _, peak_kind = peaks
+    cfg = gdn.workloads.config(3 if wl_p == "prefill_varlen16" else 4)
+    seqlens = list(cfg.seqlens)
+    if wl_p == "prefill_8x32768" and world > 1:
+        plan = gdn.sharding.plan_prefill(seqlens, 32, world)
+        seqlens = [seqlens[i] for i in plan[rank].seqs]
+    psets = prefill_sets(gdn, seqlens, 2, seed=rank, device="cuda", zero_state=cfg.zero_state)
+    sampler = ClockSampler(local)
+    pms, plaunch = time_steps(lambda s: prefill_call(gdn, s), psets, steps, warmup, world, sampler)
+    tokens = sum_over_ranks(sum(seqlens), world)
+    flops_launch = gdn.workloads.prefill_flops_per_token() * sum(seqlens)
+    traffic = profile_traffic(f"gdn_{wl_p}")
+    res = {"workload": wl_p, "tokens_per_s": tokens / (pms * 1e-3), "ms_per_step": pms, "steps": steps,
+           "tokens_per_rank": sum(seqlens), "num_seqs_per_rank": len(seqlens),
+           "scaling": "strong" if wl_p == "prefill_8x32768" else "weak",
+           "roofline": {"bound": "tensor", "achieved": flops_launch / (plaunch * 1e-3) / 1e12,
+                        "peak": bf16_peak, "unit": "TFLOP/s",
+                        "frac": flops_launch / (plaunch * 1e-3) / 1e12 / bf16_peak,
+                        "peak_kind": f"{peak_kind} bf16_tflops (burst)",
+                        "kernel": "one prefill step (every kernel of the call): algorithmic FLOPs / step time",
+                        "hbm_gbs": gdn.workloads.prefill_bytes(sum(seqlens), len(seqlens)) / (plaunch * 1e-3) / 1e9,
+                        "traffic": traffic,
+                        "traffic_source": f"profiles/gdn_{wl_p}.txt" if traffic is not None else None,
+                        "avg_launch_us": plaunch * 1e3},
+           "gpu_launches_per_step": prefill_launches(gdn, seqlens),
+           "clocks": sampler.summary()}
+    del psets
+    torch.cuda.empty_cache()
+    return res, seqlens
+
+
+def cpu_torch_reference(budget_s: float):
+    """The definition's torch reference recurrence (flashinfer 0.6.11.post2,
+    ``flashinfer/trace/templates/gdn.py``) on the host cores: configs[0] (decode B = 1)
+    and a prefill sample.  Returns a dict, or the reason it could not run."""
+    try:
+        from flashinfer.trace.templates.gdn import _gdn_decode_reference, _gdn_prefill_reference
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer torch reference not importable: {type(e).__name__}: {e}"[:200]}
+    gdn = load_package()
+    cores = os.cpu_count() or 1
+    old = torch.get_num_threads()
+    torch.set_num_threads(cores)
+    try:
+        inp = gdn.workloads.decode_inputs(1, seed=0)
+        args = (inp["q"], inp["k"], inp["v"], inp["state"], inp["A_log"], inp["a"], inp["dt_bias"], inp["b"],
+                inp["scale"])
+        _gdn_decode_reference(*args)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s / 2:
+            _gdn_decode_reference(*args)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        dec = {"workload": "configs[0] decode B=1", "ms_per_step": dt * 1e3,
+               "gbs": gdn.workloads.decode_bytes_per_seq() / dt / 1e9, "reps": reps}
+        pin = gdn.workloads.prefill_inputs([64], seed=0)
+        pargs = (pin["q"], pin["k"], pin["v"], pin["state"], pin["A_log"], pin["a"], pin["dt_bias"], pin["b"],
+                 pin["cu_seqlens"], pin["scale"])
+        t0 = time.perf_counter()
+        _gdn_prefill_reference(*pargs)
+        dt = time.perf_counter() - t0
+        pre = {"workload": "prefill sample: 1 sequence x 64 tokens (16/32 heads)", "tokens_per_s": 64 / dt,
+               "seconds": dt}
+        return {"impl": "flashinfer 0.6.11.post2 _gdn_decode_reference / _gdn_prefill_reference (torch, CPU)",
+                "cores": cores, "torch_threads": cores, "decode": dec, "prefill": pre}
+    finally:
+        torch.set_num_threads(old)
+
+
+def _load_by_path(name: str, path: Path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _time_graph(call, sets, steps, warmup):
+    """Device time per call: ``steps`` calls captured into one CUDA graph (first replay
+    untimed), CUDA events around one replay; eager back-to-back calls if capture fails."""
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        call(sets[i % len(sets)])
+    torch.cuda.synchronize()
+    g, how = None, "graph"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                call(sets[i % len(sets)])
+        g.replay()
+        torch.cuda.synchronize()
+    except Exception:  # noqa: BLE001
+        g, how = None, "eager"
+        torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record(stream)
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(steps):
+            call(sets[i % len(sets)])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return t0.elapsed_time(t1) / steps, how
+
+
+def qk4v8_prefill_lens(total: int = 8192, num_seqs: int = 32, seed: int = 8):
+    """A seeded multi-sequence prefill of ``total`` tokens, like the reference's
+    8192-token workloads (20-57 sequences)."""
+    gen = torch.Generator().manual_seed(seed)
+    w = torch.rand(num_seqs, generator=gen) + 0.05
+    lens = [max(1, int(x)) for x in (w / w.sum() * total)]
+    lens[-1] += total - sum(lens)
+    return lens
+
+
+def reference_triton_leg(gdn, steps):
+    """The reference's own sm_100 Triton kernels on this GPU beside this library, same
+    inputs and the same timing protocol (value-returning ``run`` of both, K calls in one
+    CUDA graph, rotating input sets larger than L2 where the state is large)."""
+    root = ROOT / "baseline" / "_ref" / "solution" / "triton"
+    if not (root / "kernel_decode.py").exists():
+        return {"unavailable": "reference Triton kernels not staged in baseline/_ref (run __graft_entry__.build() "
+                               "where the reference checkout is present)"}
+    try:
+        import triton  # noqa: F401
+        kd = _load_by_path("gdn_ref_kernel_decode", root / "kernel_decode.py")
+        kp = _load_by_path("gdn_ref_kernel_prefill", root / "kernel_prefill.py")
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference Triton kernels do not load on this box: {type(e).__name__}: {e}"[:300]}
+    K = max(10, min(steps, 50))
+    out = {"source": "solution/triton/kernel_decode.py::run, kernel_prefill.py::run (unmodified, staged copy)",
+           "timing": f"{K} calls of each arm's value-returning run() captured in one CUDA graph, CUDA events "
+                     "around one replay (eager back-to-back calls if capture fails)"}
+
+    def dec_case(name, B, HQ, HV):
+        one = gdn.workloads.decode_inputs(B, num_qk_heads=HQ, num_v_heads=HV, seed=3, device="cuda")
+        per_set = sum(v.numel() * v.element_size() for v in one.values() if torch.is_tensor(v))
+        n = max(2, math.ceil(3 * L2_BYTES / per_set))
+        sets = [one] + [gdn.workloads.decode_inputs(B, num_qk_heads=HQ, num_v_heads=HV, seed=3 + i, device="cuda")
+                        for i in range(1, n)]
+        keys = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "scale")
+        ref_ms, ref_how = _time_graph(lambda s: kd.run(*[s[k] for k in keys]), sets, K, 3)
+        our_ms, our_how = _time_graph(lambda s: gdn.kernel_decode.run(*[s[k] for k in keys]), sets, K, 3)
+        nbytes = gdn.workloads.decode_bytes_per_seq(HQ, HV) * B
+        out[name] = {"batch": B, "heads_qk_v": [HQ, HV], "rotating_sets": n,
+                     "reference_us": ref_ms * 1e3, "ours_us": our_ms * 1e3,
+                     "reference_gbs": nbytes / (ref_ms * 1e-3) / 1e9, "ours_gbs": nbytes / (our_ms * 1e-3) / 1e9,
+                     "speedup": ref_ms / our_ms, "capture": [ref_how, our_how]}
+        del sets
+        torch.cuda.empty_cache()
+
+    def pre_case(name, lens, HQ, HV):
+        sets = [gdn.workloads.prefill_inputs(lens, num_qk_heads=HQ, num_v_heads=HV, seed=5 + i, device="cuda")
+                for i in range(2)]
+        keys = ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens", "scale")
+        kk = max(3, K // 5)
+        ref_ms, ref_how = _time_graph(lambda s: kp.run(*[s[k] for k in keys]), sets, kk, 2)
+        our_ms, our_how = _time_graph(lambda s: gdn.kernel_prefill.run(*[s[k] for k in keys]), sets, kk, 2)
+        T = sum(lens)
+        out[name] = {"num_seqs": len(lens), "tokens": T, "heads_qk_v": [HQ, HV],
+                     "reference_ms": ref_ms, "ours_ms": our_ms,
+                     "reference_tokens_per_s": T / (ref_ms * 1e-3), "ours_tokens_per_s": T / (our_ms * 1e-3),
+                     "speedup": ref_ms / our_ms, "capture": [ref_how, our_how]}
+        del sets
+        torch.cuda.empty_cache()
+
+    try:
+        dec_case("configs1_decode_b64", 64, 16, 32)
+        for B in (1, 8, 64):
+            dec_case(f"qk4v8_decode_b{B}", B, 4, 8)
+        pre_case("configs3_prefill_varlen16", list(gdn.workloads.config(3).seqlens), 16, 32)
+        pre_case("qk4v8_prefill_8192", qk4v8_prefill_lens(), 4, 8)
+    except Exception as e:  # noqa: BLE001
+        out["error"] = f"{type(e).__name__}: {e}"[:300]
+    return out
+
+
 # ----------------------------------------------------------------------------- main
 def run_reference(args, world, rank):
     """Reference arm: the reference algorithm's CPU implementation (the C
@@ -473,68 +714,53 @@ def run_reference(args, world, rank):
 
 def run_ours(args, world, rank, local):
     gdn = load_package()
-    hbm_peak, bf16_peak, bf16_sust, peak_kind = measured_peaks()
+    peaks = measured_peaks()
+    hbm_peak, bf16_peak, bf16_sust, peak_kind = peaks
     wl = args.workload
     result = {}
+    legs = args.legs and wl == "decode_b64"
+    leg_warm = max(3, min(args.warmup, 10))
     if wl.startswith("decode"):
-        batch = 64 if wl == "decode_b64" else 1024 // world
-        one = decode_sets(gdn, batch, 1, seed=rank, device="cuda")
-        n_sets = max(2, math.ceil(3 * L2_BYTES / set_bytes(one[0])))
-        sets = one + decode_sets(gdn, batch, n_sets - 1, seed=rank + 1, device="cuda")
-        sampler = ClockSampler(local)
-        ms, launch_ms = time_steps(lambda s: decode_call(gdn, s), sets, args.steps, args.warmup, world, sampler,
-                                   graph=True)
-        bytes_rank = gdn.workloads.decode_bytes_per_seq() * batch
-        total_bytes = sum_over_ranks(bytes_rank, world)
-        value = total_bytes / (ms * 1e-3) / 1e9
-        achieved = bytes_rank / (launch_ms * 1e-3) / 1e9
-        e2e_steps = max(3, min(20, args.steps // 50))
-        e2e_ms, h2d, d2h = decode_e2e(gdn, batch, e2e_steps, 2, world, seed=rank)
-        result.update(
-            metric="GDN decode state GB/s", value=value, unit="GB/s", ms_per_step=ms, dtype="f32",
-            config={"workload": wl, "batch_per_rank": batch, "num_qk_heads": 16, "num_v_heads": 32,
-                    "head_dim": 128, "state": "fp32 k-last", "rotating_buffer_sets": len(sets),
-                    "l2": f"inputs larger than L2: {len(sets)} rotating sets, "
-                          f"{len(sets) * set_bytes(sets[0]) / 1e6:.0f} MB footprint",
-                    "parallelism": f"dp{world} (sequences sharded, no collective)",
-                    "timing": "the K steps replayed from one CUDA graph (the serving form of a decode loop); "
-                              "CUDA events around the timed region only"},
-            roofline={"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                      "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)",
-                      "traffic": profile_traffic("gdn_decode_b64"),
-                      "kernel": "decode_kernel", "avg_launch_us": launch_ms * 1e3,
-                      "algorithmic_bytes_per_launch": bytes_rank},
-            e2e={"value": total_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                 "path": "kernel_decode.run_dps() with pinned host inputs and outputs (state in and out every step); copies in, decode and copies out on three streams over two device buffer sets"},
-            gpu_launches=args.steps,
-            clocks=sampler.summary())
-        del sets
-    if wl.startswith("decode") or wl == "mtp_b64_t4":
+        d = decode_leg(gdn, wl, world, rank, local, args.steps, args.warmup, peaks, with_e2e=True)
+        cfg = {"workload": wl, "batch_per_rank": d["batch_per_rank"], "num_qk_heads": 16, "num_v_heads": 32,
+               "head_dim": 128, "state": "fp32 k-last", "rotating_buffer_sets": d["rotating_buffer_sets"],
+               "l2": d["l2"], "parallelism": f"dp{world} (sequences sharded, no collective)",
+               "timing": "the K steps replayed from one CUDA graph (the serving form of a decode loop); "
+                         "CUDA events around the timed region only"}
+        result.update(metric="GDN decode state GB/s", value=d["gbs"], unit="GB/s", ms_per_step=d["ms_per_step"],
+                      dtype="f32", config=cfg, roofline=d["roofline"], e2e=d["e2e"], gpu_launches=args.steps,
+                      clocks=d["clocks"], scaling=d["scaling"])
+        if legs:
+            result["decode_b1024"] = decode_leg(gdn, "decode_b1024", world, rank, local, leg_steps(args.steps, 200),
+                                                leg_warm, peaks, with_e2e=False)
+    if legs or wl == "mtp_b64_t4":
         # pooled multi-token decode (serving form): 64 sequences x 4 tokens per call, in place
         mb, mt = 64, 4
         msets = mtp_sets(gdn, mb, mt, 3, seed=rank + 7, device="cuda")
-        msteps = args.steps if wl == "mtp_b64_t4" else max(20, min(200, args.steps // 10))
-        mwarm = args.warmup if wl == "mtp_b64_t4" else 5
-        sampler_m = ClockSampler(local) if wl == "mtp_b64_t4" else None
+        msteps = args.steps if wl == "mtp_b64_t4" else leg_steps(args.steps, 200)
+        mwarm = args.warmup if wl == "mtp_b64_t4" else leg_warm
+        sampler_m = ClockSampler(local)
         mms, mlaunch = time_steps(lambda s: mtp_call(gdn, s), msets, msteps, mwarm, world, sampler_m, graph=True)
         mbytes = gdn.workloads.mtp_bytes_per_seq(mt) * mb
         mres = {"workload": "mtp_b64_t4", "gbs": sum_over_ranks(mbytes, world) / (mms * 1e-3) / 1e9,
-                "tokens_per_s": sum_over_ranks(mb * mt, world) / (mms * 1e-3), "ms_per_step": mms,
+                "tokens_per_s": sum_over_ranks(mb * mt, world) / (mms * 1e-3), "ms_per_step": mms, "steps": msteps,
                 "roofline": {"bound": "hbm", "achieved": mbytes / (mlaunch * 1e-3) / 1e9, "peak": hbm_peak,
                              "unit": "GB/s", "frac": mbytes / (mlaunch * 1e-3) / 1e9 / hbm_peak,
-                             "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)", "kernel": "decode_mtp_kernel",
-                             "avg_launch_us": mlaunch * 1e3, "algorithmic_bytes_per_launch": mbytes}}
+                             "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)", "kernel": "decode_mtp_pipe_kernel",
+                             "traffic": profile_traffic("gdn_decode_mtp_b64_t4"),
+                             "avg_launch_us": mlaunch * 1e3, "algorithmic_bytes_per_launch": mbytes},
+                "clocks": sampler_m.summary()}
         if wl == "mtp_b64_t4":
             result.update(metric="GDN multi-token decode state GB/s", value=mres["gbs"], unit="GB/s",
                           ms_per_step=mms, dtype="f32",
                           config={"workload": wl, "batch_per_rank": mb, "tokens_per_seq": mt,
                                   "pool_slots": 3 * mb, "l2": "3 disjoint slot sets, 805 MB pool",
                                   "parallelism": f"dp{world}"},
-                          roofline=mres["roofline"], gpu_launches=msteps, clocks=sampler_m.summary(), e2e=None)
+                          roofline=mres["roofline"], gpu_launches=msteps, clocks=mres["clocks"], e2e=None)
         else:
             result["mtp"] = mres
         del msets
+        torch.cuda.empty_cache()
     if wl == "longctx_1x131072":
         # one 131,072-token sequence (all 32 v-heads): 1 GPU = the prefill with its in-GPU
         # context-parallel segments; N GPUs = context parallelism across ranks (strong scaling:
@@ -546,7 +772,7 @@ def run_ours(args, world, rank, local):
             inp["output"] = torch.empty(L, 32, 128, dtype=torch.bfloat16, device="cuda")
             inp["new_state"] = torch.empty_like(inp["state"])
             call = lambda s: prefill_call(gdn, s)  # noqa: E731
-            local_tokens, launches = L, 4  # prep, pass 1, combine, reruns
+            local_tokens, launches = L, prefill_launches(gdn, seqlens)
         else:
             loc = gdn.context_parallel.local_inputs(inp, world, rank)
             inp = loc
@@ -556,7 +782,7 @@ def run_ours(args, world, rank, local):
                 cp.prefill_context_parallel(s["q"], s["k"], s["v"], s["state"], s["A_log"], s["a"], s["dt_bias"],
                                             s["b"], s["cu_seqlens"], s["scale"])
             local_tokens = int(loc["q"].shape[0])
-            launches = 4 if rank == 0 else 7  # rank 0: prefill; others: map (prep, chains, combine) + prefill
+            launches = prefill_launches(gdn, [local_tokens]) + (0 if rank == 0 else 3)
         sampler_l = ClockSampler(local)
         lms, llaunch = time_steps(call, [inp], args.steps, args.warmup, world, sampler_l)
         flops = gdn.workloads.prefill_flops_per_token() * L
@@ -570,53 +796,33 @@ def run_ours(args, world, rank, local):
                                 "unit": "TFLOP/s", "frac": flops / (lms * 1e-3) / 1e12 / world / bf16_peak,
                                 "peak_kind": f"{peak_kind} bf16_tflops (burst)",
                                 "note": "whole step per GPU (all kernels and collectives), algorithmic FLOPs"},
-                      gpu_launches=launches * args.steps, clocks=sampler_l.summary(), e2e=None)
-        result["scaling"] = "strong"
+                      gpu_launches=launches * args.steps, clocks=sampler_l.summary(), e2e=None, scaling="strong")
         del inp
-    if args.prefill and not wl.startswith("prefill") and wl not in ("mtp_b64_t4", "longctx_1x131072"):
-        wl_p = "prefill_varlen16"
-    elif wl.startswith("prefill"):
-        wl_p = wl
-    else:
-        wl_p = None
-    if wl_p:
-        cfg = gdn.workloads.config(3 if wl_p == "prefill_varlen16" else 4)
-        seqlens = list(cfg.seqlens)
-        if wl_p == "prefill_8x32768" and world > 1:
-            plan = gdn.sharding.plan_prefill(seqlens, 32, world)
-            seqlens = [seqlens[i] for i in plan[rank].seqs]
-        psets = prefill_sets(gdn, seqlens, 2, seed=rank, device="cuda", zero_state=cfg.zero_state)
-        psteps = max(3, min(20, args.steps // 100)) if not wl.startswith("prefill") else args.steps
-        pwarm = 2 if not wl.startswith("prefill") else args.warmup
-        sampler_p = ClockSampler(local) if wl.startswith("prefill") else None
-        pms, plaunch = time_steps(lambda s: prefill_call(gdn, s), psets, psteps, pwarm, world, sampler_p)
-        tokens = sum_over_ranks(sum(seqlens), world)
-        flops_launch = gdn.workloads.prefill_flops_per_token() * sum(seqlens)
-        pres = {"workload": wl_p, "tokens_per_s": tokens / (pms * 1e-3), "ms_per_step": pms,
-                "tokens_per_rank": sum(seqlens), "num_seqs_per_rank": len(seqlens),
-                "roofline": {"bound": "tensor", "achieved": flops_launch / (plaunch * 1e-3) / 1e12,
-                             "peak": bf16_peak, "unit": "TFLOP/s",
-                             "frac": flops_launch / (plaunch * 1e-3) / 1e12 / bf16_peak,
-                             "peak_kind": f"{peak_kind} bf16_tflops (burst)",
-                             "hbm_gbs": gdn.workloads.prefill_bytes(sum(seqlens), len(seqlens))
-                             / (plaunch * 1e-3) / 1e9,
-                             "traffic": profile_traffic("gdn_prefill_varlen16"),
-                             "avg_launch_us": plaunch * 1e3}}
+        torch.cuda.empty_cache()
+    prefill_legs = []
+    if wl.startswith("prefill"):
+        prefill_legs.append((wl, args.steps, args.warmup))
+    elif legs and args.prefill:
+        prefill_legs += [("prefill_varlen16", leg_steps(args.steps, 50), leg_warm),
+                         ("prefill_8x32768", leg_steps(args.steps, 20), leg_warm)]
+    cpu_seqlens = None
+    for wl_p, psteps, pwarm in prefill_legs:
+        pres, seqlens = prefill_leg(gdn, wl_p, world, rank, local, psteps, pwarm, peaks)
+        if wl_p == "prefill_varlen16":
+            cpu_seqlens = seqlens
         if wl.startswith("prefill"):
             result.update(metric="GDN prefill tokens/s", value=pres["tokens_per_s"], unit="tokens/s",
-                          ms_per_step=pms, dtype="bf16", config={"workload": wl_p, "seqlens_per_rank": seqlens,
-                                                                 "parallelism": f"dp{world}"},
-                          roofline=pres["roofline"], gpu_launches=prefill_launches(gdn, seqlens) * psteps,
-                          clocks=sampler_p.summary(),
-                          e2e=None)
-            if wl_p == "prefill_8x32768":
-                # configs[4] is one fixed batch of 8 sequences split over the ranks (strong scaling)
-                result["scaling"] = "strong"
+                          ms_per_step=pres["ms_per_step"], dtype="bf16",
+                          config={"workload": wl_p, "seqlens_per_rank": seqlens,
+                                  "l2": "inputs larger than L2 (2 rotating sets)",
+                                  "parallelism": f"dp{world}" + (" (sequences split over the ranks)"
+                                                                 if wl_p == "prefill_8x32768" else "")},
+                          roofline=pres["roofline"], gpu_launches=pres["gpu_launches_per_step"] * psteps,
+                          clocks=pres["clocks"], e2e=None, scaling=pres["scaling"])
         else:
-            result["prefill"] = pres
-        del psets
+            result["prefill" if wl_p == "prefill_varlen16" else wl_p] = pres
     if rank == 0:
-        budget = float(os.environ.get("GDN_BENCH_CPU_BUDGET_S", "10"))
+        budget = float(os.environ.get("GDN_BENCH_CPU_BUDGET_S", "8"))
         if world == 1 and budget > 0:
             if wl.startswith("decode"):
                 v, sample, cores = cpu_decode_rate(gdn, 64 if wl == "decode_b64" else 1024, budget)
@@ -626,10 +832,18 @@ def run_ours(args, world, rank, local):
                 v, sample, cores = cpu_mtp_rate(gdn, 64, 4, budget)
                 result["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
                                           "sample": sample}
-            else:
-                v, sample, cores = cpu_prefill_rate(gdn, seqlens, budget)
+            elif wl.startswith("prefill"):
+                v, sample, cores = cpu_prefill_rate(gdn, result["config"]["seqlens_per_rank"], budget)
                 result["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                                           "sample": sample}
+            if cpu_seqlens is not None and "prefill" in result:
+                v, sample, cores = cpu_prefill_rate(gdn, cpu_seqlens, budget)
+                result["prefill"]["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                                     "sample": sample}
+            if legs:
+                result["cpu_torch_reference"] = cpu_torch_reference(budget)
+        if world == 1 and legs and args.reference_triton:
+            result["reference_triton"] = reference_triton_leg(gdn, args.steps)
         line = {"metric": result["metric"], "value": result["value"], "unit": result["unit"],
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": result["ms_per_step"], "higher_is_better": True,
@@ -649,7 +863,11 @@ def main():
                     choices=["decode_b64", "decode_b1024", "prefill_varlen16", "prefill_8x32768", "mtp_b64_t4",
                              "longctx_1x131072"])
     ap.add_argument("--no-prefill", dest="prefill", action="store_false",
-                    help="skip the secondary configs[3] prefill measurement")
+                    help="skip the configs[3] and configs[4] prefill legs of the default line")
+    ap.add_argument("--no-legs", dest="legs", action="store_false",
+                    help="the headline decode only (no configs[2] / prefill / mtp / CPU / reference legs)")
+    ap.add_argument("--no-reference-triton", dest="reference_triton", action="store_false",
+                    help="skip timing the reference's Triton kernels on the GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

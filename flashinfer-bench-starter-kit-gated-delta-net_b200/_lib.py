@@ -21,6 +21,7 @@ GDN_ERR_WORKSPACE = 4
 GDN_FLAG_QK_L2NORM = 0x1
 GDN_FLAG_PREFILL_SERIAL = 0x2
 GDN_FLAG_STATE_MAP = 0x4
+GDN_FLAG_SELFTEST_WAIT_TIMEOUT = 0x80000000
 
 
 def GDN_PREFILL_SEGMENTS(n: int) -> int:

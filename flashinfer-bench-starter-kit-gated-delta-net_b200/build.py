@@ -3,7 +3,9 @@
 The library is written next to this file so it travels with the source tree;
 intermediate objects go to ``_build/``.  Sources are compiled in parallel with
 relocatable device code and device-linked into one shared object that exports
-only the C ABI of ``include/gdn_b200.h``.
+only the C ABI of ``include/gdn_b200.h``.  When ``tvm_ffi`` is installed, the
+TVM-FFI module ``libgdn_b200_tvm_ffi.so`` (``csrc/gdn_tvm_ffi.cc``, host C++
+over that C ABI) is built next to it.
 
     python build.py [--force] [--verbose]
 """
@@ -43,7 +45,7 @@ def sources() -> list[Path]:
 
 
 def _deps_mtime() -> float:
-    files = list(CSRC.glob("*")) + list(INCLUDE.glob("*.h")) + [Path(__file__)]
+    files = [f for f in CSRC.glob("*") if f.suffix != ".cc"] + list(INCLUDE.glob("*.h")) + [Path(__file__)]
     return max(f.stat().st_mtime for f in files if f.is_file())
 
 
@@ -64,8 +66,50 @@ def _compile(src: Path, verbose: bool) -> Path:
     return obj
 
 
+TVM_SRC = CSRC / "gdn_tvm_ffi.cc"
+TVM_LIB_PATH = HERE / "libgdn_b200_tvm_ffi.so"
+
+
+def tvm_ffi_paths():
+    """(include dirs, lib dir) of the installed tvm_ffi package, or None if it is absent."""
+    try:
+        import tvm_ffi.libinfo as info
+    except ImportError:
+        return None
+    lib = Path(info.find_libtvm_ffi()).parent
+    return [str(p) for p in info.include_paths()], str(lib)
+
+
+def build_tvm_ffi(force: bool = False) -> Path | None:
+    """The TVM-FFI module (host C++ over the C ABI), when tvm_ffi is installed."""
+    paths = tvm_ffi_paths()
+    if paths is None:
+        return None
+    if not force and TVM_LIB_PATH.exists() and TVM_LIB_PATH.stat().st_mtime >= max(
+            TVM_SRC.stat().st_mtime, LIB_PATH.stat().st_mtime, (INCLUDE / "gdn_b200.h").stat().st_mtime):
+        return TVM_LIB_PATH
+    incs, libdir = paths
+    cuda = Path(nvcc()).resolve().parent.parent
+    tmp = TVM_LIB_PATH.with_suffix(".so.tmp")
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", *[f"-I{i}" for i in incs], f"-I{cuda / 'include'}",
+           str(TVM_SRC), "-o", str(tmp), f"-L{HERE}", "-lgdn_b200", "-Wl,-rpath,$ORIGIN",
+           f"-L{libdir}", "-ltvm_ffi", f"-Wl,-rpath,{libdir}", f"-L{cuda / 'lib64'}", "-lcudart",
+           f"-Wl,-rpath,{cuda / 'lib64'}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"TVM-FFI module build failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, TVM_LIB_PATH)
+    return TVM_LIB_PATH
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile and link the library if any source is newer than it."""
+    """Compile and link the library if any source is newer than it, then the TVM-FFI module."""
+    _build_lib(force, verbose)
+    build_tvm_ffi(force)
+    return LIB_PATH
+
+
+def _build_lib(force: bool, verbose: bool) -> Path:
     if not force and not is_stale():
         return LIB_PATH
     BUILD_DIR.mkdir(exist_ok=True)

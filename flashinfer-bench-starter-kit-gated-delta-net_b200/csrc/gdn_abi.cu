@@ -124,7 +124,8 @@ int gdn_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, const void
   if (rc) return rc;
   if (batch < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "batch must be >= 0 (got %d)", batch);
   if (batch > 65535) return fail(GDN_ERR_UNSUPPORTED, "batch > 65535 per call is not supported (got %d)", batch);
-  if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
+  if (flags & ~(GDN_FLAG_QK_L2NORM | GDN_FLAG_SELFTEST_WAIT_TIMEOUT))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
   if (batch == 0) return ok();
   if (!q || !k || !v || !A_log || !a || !dt_bias || !b || !out)
     return fail(GDN_ERR_INVALID_ARGUMENT, "a required tensor pointer is NULL");
@@ -199,7 +200,8 @@ int gdn_decode_pooled(const void* q, int64_t q_stride_b, int64_t q_stride_t, int
   if (batch < 0 || tokens < 0)
     return fail(GDN_ERR_INVALID_ARGUMENT, "batch and tokens must be >= 0 (got %d, %d)", batch, tokens);
   if (batch > 65535) return fail(GDN_ERR_UNSUPPORTED, "batch > 65535 per call is not supported (got %d)", batch);
-  if (flags & ~GDN_FLAG_QK_L2NORM) return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
+  if (flags & ~(GDN_FLAG_QK_L2NORM | GDN_FLAG_SELFTEST_WAIT_TIMEOUT))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags);
   if (batch == 0 || tokens == 0) return ok();
   if (pool_size <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "pool_size must be positive (got %d)", pool_size);
   if (!q || !k || !v || !pool || !indices || !A_log || !a || !dt_bias || !b || !out)

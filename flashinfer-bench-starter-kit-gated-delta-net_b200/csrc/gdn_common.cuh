@@ -97,8 +97,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t 
 }
 
 // Wait for the phase with the given parity to complete. Returns false (and
-// records kDevErrWaitTimeout) if it does not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// records kDevErrWaitTimeout) if it does not complete within limit_ns
+// (kWaitLimitNs unless a caller asks for less).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   const uint32_t addr = smem_u32(bar);
 #pragma unroll 1
   for (int i = 0; i < 256; ++i)
@@ -107,7 +109,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       raise_device_error(kDevErrWaitTimeout);
       return false;
     }

@@ -39,6 +39,20 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeParams p) {
   const int lane = threadIdx.x & 31;
   const bool has_state = p.state != nullptr;
 
+  if (p.flags & kFlagSelftestWaitTimeout) {
+    // Self-test of the bounded-wait path: every thread waits on a barrier that nothing
+    // arrives at, with a 1 ms limit.  No copy is issued, so nothing is in flight when the
+    // waits give up; each records GDN_DEVERR_WAIT_TIMEOUT and the CTA returns without
+    // touching out / new_state.
+    if (threadIdx.x == 0) {
+      mbar_init(&bars[0], 1);
+      fence_barrier_init();
+    }
+    __syncthreads();
+    mbar_wait(&bars[0], 0, kSelftestWaitLimitNs);  // gives up: the phase cannot complete
+    return;
+  }
+
   const size_t in_off = (size_t)bi * p.s_sb + (size_t)h * p.s_sh + (size_t)row0 * kHeadDim;
   if (threadIdx.x == 0 && has_state) {
 #pragma unroll

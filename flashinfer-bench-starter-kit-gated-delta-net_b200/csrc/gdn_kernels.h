@@ -9,6 +9,9 @@ namespace gdn {
 
 constexpr uint32_t kFlagQkL2Norm = 1u;        // mirrors GDN_FLAG_QK_L2NORM
 constexpr uint32_t kFlagPrefillSerial = 2u;   // mirrors GDN_FLAG_PREFILL_SERIAL
+constexpr uint32_t kFlagSelftestWaitTimeout = 1u << 31;  // mirrors GDN_FLAG_SELFTEST_WAIT_TIMEOUT
+// Wait limit of the self-test: long enough to leave the fast spin, short enough for a test.
+constexpr unsigned long long kSelftestWaitLimitNs = 1000000ull;  // 1 ms
 
 // Strides are in elements; the innermost (feature) stride is 1 for every tensor.
 struct DecodeParams {

@@ -48,9 +48,10 @@ def _flags(use_qk_l2norm: bool) -> int:
 
 
 def run_dps(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, *,
-            use_qk_l2norm: bool = False):
+            use_qk_l2norm: bool = False, extra_flags: int = 0):
     """Destination-passing decode: writes ``output`` [B,1,HV,128] bf16 and
-    ``new_state`` [B,HV,128,128] fp32 (which may be ``state`` itself)."""
+    ``new_state`` [B,HV,128,128] fp32 (which may be ``state`` itself).
+    ``extra_flags`` are further C-ABI flag bits (``GDN_FLAG_SELFTEST_WAIT_TIMEOUT``)."""
     B, T1, HQ, D = q.shape
     HV = v.shape[2]
     if T1 != 1:
@@ -75,7 +76,7 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, *,
                         ptr(A_log), ptr(a), a.stride(0), ptr(dt_bias), ptr(b), b.stride(0),
                         float(scale),
                         ptr(output), *so, ptr(new_state), *sn,
-                        B, HQ, HV, D, _flags(use_qk_l2norm), stream_handle(q.device))
+                        B, HQ, HV, D, _flags(use_qk_l2norm) | int(extra_flags), stream_handle(q.device))
     _lib.check(rc)
     return output, new_state
 

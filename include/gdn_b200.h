@@ -55,6 +55,11 @@ extern "C" {
 #define GDN_PREFILL_SEGMENTS(n) ((((uint32_t)(n)) & 15u) << 8)
 /* gdn_prefill_workspace_size: size the workspace of gdn_prefill_state_map instead. */
 #define GDN_FLAG_STATE_MAP 0x4u
+/* gdn_decode self-test of the device-side failure path: every thread of the launch waits
+ * on a barrier that nothing completes, gives up after 1 ms, records
+ * GDN_DEVERR_WAIT_TIMEOUT and returns; out and new_state are not written.  No copy or
+ * tensor-core work is in flight when the waits give up, so the context stays usable. */
+#define GDN_FLAG_SELFTEST_WAIT_TIMEOUT 0x80000000u
 
 /* Device-side error bits reported by gdn_device_error(). */
 #define GDN_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded wait inside a kernel gave up */

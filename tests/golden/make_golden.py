@@ -14,7 +14,7 @@ patterns; the initial states are drawn as bf16-representable fp32 values so
 they can be stored as uint16 too.
 
 Usage (needs the reference checkout; not run by the tests):
-    python tests/golden/make_golden.py /path/to/reference
+    python tests/golden/make_golden.py /path/to/reference [qk16v32]
 """
 from __future__ import annotations
 
@@ -28,36 +28,21 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+from seeded import (STORED_HEADS, bits, decode_qk16v32_inputs, digest, make_inputs,  # noqa: E402
+                    prefill_qk16v32_inputs)
 
 
-def bits(t: torch.Tensor) -> np.ndarray:
-    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
-
-
-def make_inputs(shape_q, shape_v, shape_g, state_shape, seed):
-    gen = torch.Generator()
-    gen.manual_seed(seed)
-
-    def unit(shape):
-        x = torch.randn(*shape, generator=gen)
-        return (x / x.norm(dim=-1, keepdim=True)).bfloat16()
-
-    q, k = unit(shape_q), unit(shape_q)
-    v = torch.randn(*shape_v, generator=gen).bfloat16()
-    a = torch.randn(*shape_g, generator=gen).bfloat16()
-    b = torch.randn(*shape_g, generator=gen).bfloat16()
-    HV = shape_v[-2]
-    A_log = torch.rand(HV, generator=gen) * 1.5
-    dt_bias = torch.rand(HV, generator=gen) * 2 - 1
-    state = (torch.randn(*state_shape, generator=gen) * 0.05).bfloat16().float()
-    return q, k, v, a, b, A_log, dt_bias, state
-
-
-def main(ref_root: str) -> None:
+def main(ref_root: str, only: str | None = None) -> None:
     sys.path.insert(0, str(Path(ref_root) / "solution" / "triton"))
     import kernel_decode  # reference decode entry point
     import kernel_prefill  # reference prefill entry point
     from flashinfer.trace.templates.gdn import _gdn_decode_reference, _gdn_mtp_reference, _gdn_prefill_reference
+
+    if only in (None, "qk16v32"):
+        make_qk16v32(kernel_decode, kernel_prefill, _gdn_decode_reference, _gdn_prefill_reference)
+    if only == "qk16v32":
+        return
 
     # ---- decode, the reference definition's own head counts (qk4 / v8) ----
     cases = [("decode_qk4v8_b3", 3, 4, 8, 11, True, None),
@@ -118,7 +103,41 @@ def main(ref_root: str) -> None:
           bool(torch.equal(pool_fi[0], pool[0]) and torch.equal(pool_fi[2], pool[2])))
 
 
+def make_qk16v32(kernel_decode, kernel_prefill, decode_ref, prefill_ref) -> None:
+    """BASELINE.json's head counts (16 q/k heads, 32 v heads; the reference kernels hard-code
+    the GVA ratio 2, which these keep).  Inputs are regenerated from the seed by the tests
+    (``seeded.py``; the fixture keeps their digest); stored: every output and the final
+    states of the v-heads in ``STORED_HEADS``."""
+    heads = torch.tensor(STORED_HEADS)
+    q, k, v, a, b, A_log, dt_bias, state = decode_qk16v32_inputs()
+    o_tr, s_tr = kernel_decode.run(q, k, v, state, A_log, a, dt_bias, b, None)
+    o_fi, s_fi = decode_ref(q, k, v, state, A_log, a, dt_bias, b, None)
+    np.savez_compressed(
+        HERE / "decode_qk16v32_b2.npz", seed=np.int64(13), stored_heads=heads.numpy(),
+        inputs_sha256=np.array(digest(q, k, v, a, b, A_log, dt_bias, state)),
+        out_triton=bits(o_tr), new_state_triton=s_tr[:, heads].numpy(),
+        torchref_out_maxdiff=np.float32((o_tr.float() - o_fi.float()).abs().max().item()),
+        torchref_state_maxdiff=np.float32((s_tr - s_fi).abs().max().item()))
+    print("decode qk16v32 triton vs torch-ref: out", (o_tr.float() - o_fi.float()).abs().max().item(),
+          "state", (s_tr - s_fi).abs().max().item())
+
+    lens = [200, 0, 65]  # 4 chunks (3 full + 8 tokens), an empty sequence, 2 chunks (1 full + 1 token)
+    q, k, v, a, b, A_log, dt_bias, state, cu = prefill_qk16v32_inputs(lens)
+    o_tr, s_tr = kernel_prefill.run(q, k, v, state, A_log, a, dt_bias, b, cu, None)
+    o_fi, s_fi = prefill_ref(q, k, v, state, A_log, a, dt_bias, b, cu, None)
+    np.savez_compressed(
+        HERE / "prefill_qk16v32_lens200-0-65.npz", seed=np.int64(22), lens=np.array(lens),
+        stored_heads=heads.numpy(), inputs_sha256=np.array(digest(q, k, v, a, b, A_log, dt_bias, state, cu)),
+        out_triton=bits(o_tr), new_state_triton=s_tr[:, heads].numpy(),
+        torchref_out_maxdiff=np.float32((o_tr.float() - o_fi.float()).abs().max().item()),
+        torchref_state_maxdiff_nonempty=np.float32(
+            max((s_tr[i] - s_fi[i]).abs().max().item() for i in (0, 2))),
+        empty_seq_passthrough=np.array(bool(torch.equal(s_tr[1], state[1]))))
+    print("prefill qk16v32 triton vs torch-ref: out", (o_tr.float() - o_fi.float()).abs().max().item(),
+          "state (non-empty seqs)", max((s_tr[i] - s_fi[i]).abs().max().item() for i in (0, 2)))
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <reference checkout>")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        sys.exit("usage: make_golden.py <reference checkout> [qk16v32]")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) == 3 else None)

@@ -175,3 +175,15 @@ def test_invalid_arguments_raise_before_launch(gdn):
                                   inp["A_log"], inp["a"], inp["dt_bias"], inp["b"], None, out,
                                   overlap[4:].view(2, 32, 128, 128))
     del ns
+
+
+def test_golden_reference_kernel_16_32_heads(gdn):
+    """BASELINE.json's head counts (16 q/k, 32 v heads) against the reference kernel."""
+    from test_oracle import qk16v32_decode_case
+
+    g, (q, k, v, a, b, A_log, dt_bias, state) = qk16v32_decode_case()
+    dev = lambda t: t.cuda()  # noqa: E731
+    out, ns = gdn.kernel_decode.run(dev(q), dev(k), dev(v), dev(state), dev(A_log), dev(a), dev(dt_bias), dev(b),
+                                    None)
+    torch.cuda.synchronize()
+    assert_match(out, ns[:, torch.from_numpy(g["stored_heads"]).cuda()], g["out_triton"], g["new_state_triton"])

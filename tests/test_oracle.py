@@ -137,3 +137,50 @@ def test_mtp_oracle_matches_flashinfer_reference():
     assert ok, err
     untouched = [s for s in range(pool.shape[0]) if s not in set(g["indices"].tolist())]
     assert all(np.array_equal(new_pool[s], pool[s]) for s in untouched)
+
+
+# ----------------------------------------------------------------------------- 16 / 32 heads
+# BASELINE.json's head counts.  The fixtures keep the reference kernels' outputs and the
+# final states of a subset of v-heads; the inputs are regenerated from the seed
+# (tests/golden/seeded.py) and checked against the digest the fixture stores.
+from golden import seeded  # noqa: E402
+
+
+def qk16v32_decode_case():
+    g = load_golden("decode_qk16v32_b2")
+    inp = seeded.decode_qk16v32_inputs(int(g["seed"]))
+    assert seeded.digest(*inp) == str(g["inputs_sha256"]), "seeded inputs drifted from the fixture"
+    return g, inp
+
+
+def qk16v32_prefill_case():
+    g = load_golden("prefill_qk16v32_lens200-0-65")
+    inp = seeded.prefill_qk16v32_inputs([int(x) for x in g["lens"]], int(g["seed"]))
+    assert seeded.digest(*inp) == str(g["inputs_sha256"]), "seeded inputs drifted from the fixture"
+    return g, inp
+
+
+@pytest.mark.parametrize("impl", ["numpy", "c"])
+def test_decode_oracle_matches_reference_kernel_16_32_heads(impl):
+    g, (q, k, v, a, b, A_log, dt_bias, state) = qk16v32_decode_case()
+    fn = ref.decode if impl == "numpy" else c_oracle.decode
+    b16 = seeded.bits
+    out, new_state = fn(b16(q), b16(k), b16(v), state.numpy(), A_log.numpy(), b16(a), dt_bias.numpy(), b16(b), None)
+    d, m = _ulp_diff(out, g["out_triton"])
+    assert d <= 2.0 ** -7 * max(m, 1e-3)
+    ok, err = state_close(new_state[:, g["stored_heads"]], g["new_state_triton"], rtol=1e-5)
+    assert ok, err
+
+
+@pytest.mark.parametrize("impl", ["numpy", "c"])
+def test_prefill_oracle_matches_reference_kernel_16_32_heads(impl):
+    g, (q, k, v, a, b, A_log, dt_bias, state, cu) = qk16v32_prefill_case()
+    fn = ref.prefill if impl == "numpy" else c_oracle.prefill
+    b16 = seeded.bits
+    out, new_state = fn(b16(q), b16(k), b16(v), state.numpy(), A_log.numpy(), b16(a), dt_bias.numpy(), b16(b),
+                        cu.numpy(), None)
+    d, m = _ulp_diff(out, g["out_triton"])
+    assert d <= 2.0 ** -7 * max(m, 1e-3)
+    ok, err = state_close(new_state[:, g["stored_heads"]], g["new_state_triton"], rtol=1e-5)
+    assert ok, err
+    assert bool(g["empty_seq_passthrough"]) and np.array_equal(new_state[1], state[1].numpy())
