@@ -204,8 +204,7 @@ def prefill_launches(gdn, seqlens):
     if auto <= one:
         return 2
     per_state = N * 32 * 128 * 128 * 4
-    segs = round(((auto - one) // per_state + 5) / 3) if (auto - one) >= 2 * per_state else 2
-    return 4 if segs >= 3 else 3
+    return 4 if (auto - one) >= 2 * per_state else 3
 
 
 def prefill_call(gdn, s):

@@ -217,15 +217,23 @@ GDN_API size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens
 
 /*
  * gdn_prefill without a caller workspace (no counterpart in the reference, whose
- * prefill needs no scratch): the prepared chunk records live in a static device
- * array of GDN_PREFILL_NOALLOC_SCRATCH_BYTES inside the library, so the call
- * allocates nothing.  Arguments and semantics are those of gdn_prefill minus
- * the workspace.  A problem whose gdn_prefill_workspace_size(...) exceeds the
- * scratch is rejected with GDN_ERR_WORKSPACE before anything is enqueued.
- * The scratch is one per device and shared by all calls: calls on that device
- * that overlap in time (other streams or host threads) race on it.  The first
- * call on a device looks its address up (cudaGetSymbolAddress) and should come
- * before any stream capture.  No part of the scratch needs to start at zero.
+ * prefill needs no scratch), for callers that cannot allocate device memory at call
+ * time: e.g. code running inside a captured or pre-planned execution graph, or
+ * behind an allocator that must not grow.  The chunked prefill's device scratch
+ * (the prepared chunk records, and the context-parallel segments' states and maps)
+ * lives in a static device array of GDN_PREFILL_NOALLOC_SCRATCH_BYTES inside the
+ * library, so the call allocates nothing.  Arguments and semantics are those of gdn_prefill minus the
+ * workspace.  A problem whose gdn_prefill_workspace_size(...) exceeds the scratch is
+ * rejected with GDN_ERR_WORKSPACE before anything is enqueued.
+ * Footprint: the array is part of the library's device module, so every GPU on which
+ * the library's kernels are loaded holds those 64 MiB until the process exits,
+ * whether or not this entry point is ever called.
+ * The scratch is one per device and shared by all calls: calls on that device that
+ * overlap in time (other streams or host threads) race on it.  The first call on a
+ * device looks its address up (cudaGetSymbolAddress) and caches it; that call should
+ * come before any stream capture, and cudaDeviceReset while the library is loaded is
+ * not supported (the cached address would outlive the module).  No part of the
+ * scratch needs to start at zero.
  */
 #define GDN_PREFILL_NOALLOC_SCRATCH_BYTES (64u << 20)
 GDN_API int gdn_prefill_noalloc(const void* q, int64_t q_stride_t, int64_t q_stride_h,
