@@ -207,9 +207,10 @@ def prefill_launches(gdn, seqlens):
     return 4 if (auto - one) >= 2 * per_state else 3
 
 
-def prefill_call(gdn, s):
+def prefill_call(gdn, s, use_qk_l2norm=False):
     gdn.kernel_prefill.run_dps(s["q"], s["k"], s["v"], s["state"], s["A_log"], s["a"], s["dt_bias"],
-                               s["b"], s["cu_seqlens"], s["scale"], s["output"], s["new_state"])
+                               s["b"], s["cu_seqlens"], s["scale"], s["output"], s["new_state"],
+                               use_qk_l2norm=use_qk_l2norm)
 
 
 def mtp_sets(gdn, batch, tokens, n_sets, seed, device):
@@ -502,6 +503,11 @@ def prefill_leg(gdn, wl_p, world, rank, local, steps, warmup, peaks):
                         "avg_launch_us": plaunch * 1e3},
            "gpu_launches_per_step": prefill_launches(gdn, seqlens),
            "clocks": sampler.summary()}
+    if wl_p == "prefill_varlen16":
+        # the same step with q and k L2-normalised inside the kernels (use_qk_l2norm)
+        lms, _ = time_steps(lambda s: prefill_call(gdn, s, use_qk_l2norm=True), psets, steps, warmup, world)
+        res["qk_l2norm"] = {"tokens_per_s": tokens / (lms * 1e-3), "ms_per_step": lms,
+                            "relative_to_default": pms / lms}
     del psets
     torch.cuda.empty_cache()
     return res, seqlens
@@ -818,6 +824,8 @@ def run_ours(args, world, rank, local):
                                                                  if wl_p == "prefill_8x32768" else "")},
                           roofline=pres["roofline"], gpu_launches=pres["gpu_launches_per_step"] * psteps,
                           clocks=pres["clocks"], e2e=None, scaling=pres["scaling"])
+            if "qk_l2norm" in pres:
+                result["qk_l2norm"] = pres["qk_l2norm"]
         else:
             result["prefill" if wl_p == "prefill_varlen16" else wl_p] = pres
     if rank == 0:

@@ -21,8 +21,8 @@ __device__ unsigned int g_gdn_device_error = 0;
 namespace {
 
 // Scratch of gdn_prefill_noalloc: a static device array in the library's module, so that
-// entry point allocates nothing.  64 MiB holds 3,799 prepared chunk records (17,664 B each),
-// e.g. total_tokens / 64 + num_seqs + 1 <= 118 chunk slots at 32 v-heads.  No part of it needs
+// entry point allocates nothing.  64 MiB holds 3,692 prepared chunk records (18,176 B each),
+// e.g. total_tokens / 64 + num_seqs + 1 <= 115 chunk slots at 32 v-heads.  No part of it needs
 // to start at zero: the prep kernel writes every record before the chain kernel reads it.
 constexpr size_t kStaticScratchBytes = size_t(GDN_PREFILL_NOALLOC_SCRATCH_BYTES);
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
@@ -179,9 +179,9 @@ size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_
   (void)head_dim;
   // gdn_prefill_state_map: records + the per-segment maps
   if (flags & GDN_FLAG_STATE_MAP) return gdn::prefill_map_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
-  // the token-serial kernel (forced, or for in-kernel q/k normalisation) needs none;
-  // the chunked kernel keeps one prepared record per chunk slot and v-head
-  if (flags & (GDN_FLAG_PREFILL_SERIAL | GDN_FLAG_QK_L2NORM)) return 0;
+  // the token-serial kernel (forced) needs none; the chunked kernel keeps one prepared
+  // record per chunk slot and v-head (with or without in-kernel q/k normalisation)
+  if (flags & GDN_FLAG_PREFILL_SERIAL) return 0;
   return gdn::prefill_chunk_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
 }
 

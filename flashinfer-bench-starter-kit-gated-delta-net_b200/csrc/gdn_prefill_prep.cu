@@ -43,7 +43,7 @@ constexpr uint32_t kKTile = 16384;
 constexpr uint32_t kSmAT = 0;
 constexpr uint32_t kATBytes = 64 * kLd * 4;
 constexpr uint32_t kSmGate = kSmAT + 2 * kATBytes;  // per group: GA_N x 64 fp32 + scan scratch
-constexpr uint32_t kGateBytes = (GA_N + 1) * 64 * 4;
+constexpr uint32_t kGateBytes = (GA_N + 2) * 64 * 4;  // GA_N arrays + scan scratch + n_t
 constexpr uint32_t kSmBar = kSmGate + 2 * kGateBytes;
 constexpr uint32_t kSmMisc = kSmBar + 16;  // tmem base slot, per-group chunk info
 constexpr uint32_t kSmBytes = kSmMisc + 80;
@@ -283,12 +283,12 @@ __global__ void __launch_bounds__(kThreads, 4)
     }
   }
 
-  if (mine.nvalid) {
-    float* AT = reinterpret_cast<float*>(base + kSmAT + grp * kATBytes);
-    float* gates = reinterpret_cast<float*>(base + kSmGate + grp * kGateBytes);
-    unsigned char* rec = record(p, mine.slot, h);
-    // ---- gates (threads 0-63 of the group, token t = gth) ----
-    if (gth < 64) {
+  float* AT = reinterpret_cast<float*>(base + kSmAT + grp * kATBytes);
+  float* gates = reinterpret_cast<float*>(base + kSmGate + grp * kGateBytes);
+  unsigned char* rec = mine.nvalid ? record(p, mine.slot, h) : nullptr;
+  // ---- gates (threads 0-63 of the group, token t = gth) ----
+  if (mine.nvalid && gth < 64) {
+    {
       const float eA = tc::ex2_approx(p.A_log[h] * kLog2e), dt_bias = p.dt_bias[h];
       float lg = 0.f, bt = 0.f;
       if (gth < mine.nvalid) {
@@ -309,16 +309,30 @@ __global__ void __launch_bounds__(kThreads, 4)
       if (gth >= 32) x += tmp[0];
       if (gth == 63) tmp[1] = x;
       named_sync(bar64, 64);
+      // k normalisation (GDN_FLAG_QK_L2NORM): n_t = 1 / |k_t| from the chunk's K rows in
+      // shared memory, once they have landed
+      float nk = 1.f, lg2n = 0.f;
+      if ((p.flags & kFlagQkL2Norm) && mbar_wait_sleep(bar_tma, 0) && gth < mine.nvalid) {
+        const float ss = row_sumsq(base + kSmK + grp * 8192, kKTile, gth);
+        nk = l2_factor(ss);
+        lg2n = -0.5f * tc::lg2_approx(ss + 1e-6f);
+      }
       const float x2 = x * kLog2e, gC2 = tmp[1] * kLog2e;
-      const float G = tc::ex2_approx(x2);
-      const float vals[GA_N] = {x2, bt, G, bt * G, tc::ex2_approx(gC2 - x2)};
+      const float G = tc::ex2_approx(x2), GC = tc::ex2_approx(gC2);
+      const float vals[GA_N] = {x2, bt, G, bt * G * nk, tc::ex2_approx(gC2 - x2) * nk, x2 - lg2n, GC};
       float* rg = reinterpret_cast<float*>(rec + kRecT);
 #pragma unroll
       for (int a = 0; a < GA_N; ++a) {
         gates[a * 64 + gth] = vals[a];
         rg[a * 64 + gth] = vals[a];
       }
+      gates[(GA_N + 1) * 64 + gth] = bt * nk;  // row factor of A
     }
+  }
+  // the K tiles are read for the k norms by both groups before either group's A / T array
+  // overlays them
+  if (p.flags & kFlagQkL2Norm) __syncthreads();
+  if (mine.nvalid) {
     named_sync(bar128, 128);
     // ---- A rows from TMEM (the two warps whose lane quarter holds this slot's rows) ----
     int ok = 1;
@@ -336,8 +350,9 @@ __global__ void __launch_bounds__(kThreads, 4)
       tc::fence_after_sync();
       if (((warp & 3) >> 1) == grp) {
         const int t = ((warp & 1) << 5) | lane;
-        const float* g2 = gates + GA_G2 * 64;
-        const float gt = g2[t], bt = gates[GA_BETA * 64 + t];
+        // A[t][j] = beta_t n_t exp2(g2_t - (g2_j - log2 n_j)) (k_t.k_j) = beta_t exp(g_t - g_j) k^_t.k^_j
+        const float* g2 = gates + GA_G2C * 64;
+        const float gt = gates[GA_G2 * 64 + t], bt = gates[(GA_N + 1) * 64 + t];
         const uint32_t d0 = tc::tmem_addr(tmem, (uint32_t)((warp & 3) * 32), (uint32_t)(grp * 64));
 #pragma unroll 2
         for (int j8 = 0; j8 < 8; ++j8) {

@@ -68,9 +68,10 @@ def run_dps(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new
     """Destination-passing prefill: writes ``output`` [T,HV,128] bf16 and
     ``new_state`` [N,HV,128,128] fp32 (which may be ``state`` itself).
 
-    The chunked tensor-core kernel runs whenever q/k/v rows and strides are
-    16-byte aligned and ``use_qk_l2norm`` is off; otherwise (or with
-    ``serial=True``, a cross-checking switch) the token-serial CUDA kernel runs.
+    The chunked tensor-core kernel runs whenever q/k rows and strides are 16-byte
+    aligned (``use_qk_l2norm`` included: the normalisation factors are folded into
+    its per-token gate factors); otherwise (or with ``serial=True``, a
+    cross-checking switch) the token-serial CUDA kernel runs.
     ``no_alloc=True`` calls ``gdn_prefill_noalloc`` (the library's static scratch
     instead of a workspace buffer; problems larger than it are rejected).
     ``segments`` splits each sequence's chunks into that many ranges run on

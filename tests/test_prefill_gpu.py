@@ -140,3 +140,36 @@ def test_golden_reference_kernel_16_32_heads(gdn):
     torch.cuda.synchronize()
     assert_match(out, ns[:, torch.from_numpy(g["stored_heads"]).cuda()], g["out_triton"], g["new_state_triton"])
     assert torch.equal(ns[1], state[1].cuda())
+
+
+# ----------------------------------------------------------------------------- in-kernel q/k L2 norm
+def _unnormalised(inp, seed):
+    """q and k rows with random norms in [0.3, 3] (bf16), so the normalisation matters."""
+    g = torch.Generator().manual_seed(seed)
+    for key in ("q", "k"):
+        x = inp[key].float()
+        scale = 0.3 + 2.7 * torch.rand(x.shape[0], x.shape[1], 1, generator=g)
+        inp[key] = (x * scale).bfloat16()
+    return inp
+
+
+@pytest.mark.parametrize("lens", [[1000, 0, 65, 130], [3000]])
+def test_qk_l2norm_chunked_matches_oracle(gdn, lens):
+    """use_qk_l2norm on the chunked tensor-core path (the factors 1/|k_t|, 1/|q_t| folded
+    into the per-token gate factors; raw bf16 q, k in the products) against the oracle,
+    which normalises in fp32."""
+    inp = _unnormalised(gdn.workloads.prefill_inputs(lens, seed=43 + len(lens)), seed=7)
+    out, ns = gdn.kernel_prefill.run(**to_dev(inp), use_qk_l2norm=True)
+    o_ref, s_ref = oracle_prefill(inp, impl=c_oracle, use_qk_l2norm=True)
+    assert_match(out, ns, o_ref, s_ref)
+    assert gdn._lib.device_error() == 0
+
+
+def test_qk_l2norm_chunked_equals_serial(gdn):
+    inp = to_dev(_unnormalised(gdn.workloads.prefill_inputs([300, 64, 5, 0, 77], seed=44), seed=8))
+    o1, s1 = gdn.kernel_prefill.run(**inp, use_qk_l2norm=True)
+    o2, s2 = gdn.kernel_prefill.run(**inp, use_qk_l2norm=True, serial=True)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(o1.float().cpu().numpy(), o2.float().cpu().numpy(), **OUT_TOL)
+    ok, err = state_close(s1.cpu().numpy(), s2.cpu().numpy(), STATE_RTOL)
+    assert ok, err
