@@ -65,6 +65,8 @@ struct PrefillParams {
   int cp_segments = 1;
   int cp_pass = 0;
   float* cp_scratch = nullptr;
+  // GDN_FLAG_QK_L2NORM: per (token, q/k head) (1 / |q|, log2 (1 / |q|)), [T][HQ] (workspace)
+  float2* qnorm = nullptr;
   // cp_pass 2: each sequence's affine state map S_out = S_in M + C instead of a prefill
   float* map_m = nullptr;
   float* map_c = nullptr;

@@ -96,13 +96,12 @@ constexpr uint32_t kTStage = kRecT;
 constexpr uint32_t kSmP = 163840;      // P tile [64 x 64]
 constexpr uint32_t kSmO = 172032;      // output rows of one chunk, [64 tokens][128] bf16 (TMA-store source)
 constexpr uint32_t kSmGate = 188416;   // 2 stages x gate arrays (record bytes 16384-18175)
-constexpr uint32_t kSmQn = 192000;     // q normalisation of the current chunk: m_t, log2 m_t (2 x 64 fp32)
-constexpr uint32_t kSmBar = 192512;    // mbarriers (32 x 8 B)
-constexpr uint32_t kSmMisc = 192768;   // tmem base slot, abort flag
-constexpr uint32_t kSmBytes = 192832;
+constexpr uint32_t kSmBar = 192000;    // mbarriers (32 x 8 B)
+constexpr uint32_t kSmMisc = 192256;   // tmem base slot, abort flag
+constexpr uint32_t kSmBytes = 192320;
 constexpr uint32_t kSmAlloc = kSmBytes + 1024;  // + alignment slack
 static_assert(kSmKQ + 2 * kKQStage <= kSmV && kSmT + 2 * kTStage <= kSmP && kSmO + 16384 <= kSmGate &&
-                  kSmGate + 2 * kRecGates <= kSmQn && kSmQn + 512 <= kSmBar,
+                  kSmGate + 2 * kRecGates <= kSmBar,
               "smem map");
 static_assert(kSmAlloc <= 232448, "smem budget");
 
@@ -211,9 +210,6 @@ __device__ __forceinline__ bool group_wait(const Smem& sm, int bar_idx, uint32_t
 }
 
 // ---------------------------------------------------------------------------
-// L2NORM: q and k L2-normalised inside the kernel (GDN_FLAG_QK_L2NORM); a separate
-// instantiation, so the default path carries none of its registers.
-template <bool L2NORM>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_chunk_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapQ,
                          const __grid_constant__ CUtensorMap mapV, const __grid_constant__ CUtensorMap mapO,
@@ -454,7 +450,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ======================================================================= P warpgroup
   else if (warp >= kWarpP0) {
     const int pth = tid - 32 * kWarpP0;  // 0..127; TMEM lane quarter = warp & 3
-    constexpr bool l2norm = L2NORM;
     const bool pleader = pth == 0;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32);
     const int v = (warp & 3) * 32 + lane;  // state row (TMEM lane) in the O^T passes
@@ -500,24 +495,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P rows from Q K^T (D1 columns 64-127; every lane quarter holds the 64 Q rows):
       // thread (row r, column half ch) keeps P[r][32 ch .. 32 ch + 31] in registers until
       // the P tile is free; P[t][j] = exp(g_t - g_j) q_t.k_j for j <= t
-      // q normalisation (GDN_FLAG_QK_L2NORM): m_t = 1 / |q_t| from the chunk's Q rows in
-      // shared memory (the P row t and column t of S0 Q^T are scaled by it)
-      float* qm = reinterpret_cast<float*>(sm.base + kSmQn);
-      if (l2norm) {
-        if (!group_wait(sm, B_KQ_FULL + s, (i >> 1) & 1, 2, 128, pleader)) break;
-        if (pth < 64) {
-          const float ss = row_sumsq(sm.base + kSmKQ + s * kKQStage, kKQTile, pth);
-          qm[pth] = l2_factor(ss);
-          qm[64 + pth] = -0.5f * tc::lg2_approx(ss + 1e-6f);
-        }
-        named_sync(2, 128);
-      }
       const int ch = (warp & 3) >> 1, prow_r = ((warp & 1) << 5) | lane;
       uint32_t prow[16];
       {
         // P[t][j] = exp2((g2_t + log2 m_t) - (g2_j - log2 n_j)) (q_t.k_j) = exp(g_t - g_j) q^_t.k^_j
+        // (row and column terms of the gate arrays; m = n = 1 without the q/k L2 norm)
         const float* g2 = sm.gate(s, GA_G2C) + 32 * ch;
-        const float gt = sm.gate(s, GA_G2)[prow_r] + (l2norm ? qm[64 + prow_r] : 0.f);
+        const float gt = sm.gate(s, GA_G2)[prow_r];
         const uint32_t d0 = tc::tmem_addr(tmem, lane_base, d1 + 64 + 32 * ch);
 #pragma unroll
         for (int q16 = 0; q16 < 2; ++q16) {
@@ -574,11 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::tmem_wait_ld();
 #pragma unroll
           for (int u4 = 0; u4 < 4; ++u4) {
-            float4 g4 = *reinterpret_cast<const float4*>(G + q16 * 16 + 4 * u4);
-            if (l2norm) {  // column t also by m_t
-              const float4 m4 = *reinterpret_cast<const float4*>(qm + q16 * 16 + 4 * u4);
-              g4 = make_float4(g4.x * m4.x, g4.y * m4.y, g4.z * m4.z, g4.w * m4.w);
-            }
+            const float4 g4 = *reinterpret_cast<const float4*>(G + q16 * 16 + 4 * u4);
             x[4 * u4 + 0] *= g4.x;
             x[4 * u4 + 1] *= g4.y;
             x[4 * u4 + 2] *= g4.z;
@@ -980,12 +960,22 @@ size_t prefill_map_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v
   return ((records + 255) & ~(size_t)255) + (size_t)2 * S * num_seqs * num_v_heads * kStateFloats * sizeof(float);
 }
 
-size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
-  if (num_seqs <= 0 || total_tokens <= 0 || num_v_heads <= 0) return 0;
+namespace {
+// Workspace of the chunked prefill: [records][context-parallel scratch (segments)][q norms
+// (GDN_FLAG_QK_L2NORM: [T][HQ] float2, sized for HV >= HQ heads)], each part 256-byte aligned.
+size_t chunk_records_and_cp_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
   const size_t records = (size_t)chunk::num_slots(total_tokens, num_seqs) * (size_t)num_v_heads * chunk::kRecBytes;
   const int S = prefill_cp_segments(num_seqs, total_tokens, num_v_heads, flags);
   if (S <= 1) return records;
   return ((records + 255) & ~(size_t)255) + (size_t)cp_floats(num_seqs, num_v_heads, S) * sizeof(float);
+}
+}  // namespace
+
+size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  if (num_seqs <= 0 || total_tokens <= 0 || num_v_heads <= 0) return 0;
+  const size_t base = chunk_records_and_cp_bytes(num_seqs, total_tokens, num_v_heads, flags);
+  if (!(flags & kFlagQkL2Norm)) return base;
+  return ((base + 255) & ~(size_t)255) + (size_t)total_tokens * (size_t)num_v_heads * sizeof(float2);
 }
 
 bool prefill_chunk_supported(const PrefillParams& p) {
@@ -1003,10 +993,6 @@ bool prefill_chunk_supported(const PrefillParams& p) {
 }
 
 namespace {
-using ChainKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, PrefillParams);
-ChainKernel chain_kernel_for(const PrefillParams& p) {
-  return (p.flags & kFlagQkL2Norm) ? prefill_chunk_kernel<true> : prefill_chunk_kernel<false>;
-}
 // Tensor maps of one call, the prep launch and the chain kernel's shared-memory opt-in.
 // A state-map call has no output tensor: its output map is built on q (never stored to).
 cudaError_t prefill_setup(const PrefillParams& p, cudaStream_t stream, CUtensorMap* mk, CUtensorMap* mq,
@@ -1018,7 +1004,13 @@ cudaError_t prefill_setup(const PrefillParams& p, cudaStream_t stream, CUtensorM
       !make_map(mo, map_only ? const_cast<__nv_bfloat16*>(p.q) : p.out, p.T, map_only ? p.HQ : p.HV,
                 map_only ? p.q_st : p.o_st, map_only ? p.q_sh : p.o_sh, 128, false))
     return cudaErrorInvalidValue;
-  cudaError_t e = launch_prefill_prep(p, *mk, stream);
+  cudaError_t e = cudaSuccess;
+  if (p.flags & kFlagQkL2Norm) {
+    if (!p.qnorm) return cudaErrorInvalidValue;  // the q norms live in the caller's workspace
+    e = launch_qk_norm(p, stream);
+    if (e != cudaSuccess) return e;
+  }
+  e = launch_prefill_prep(p, *mk, stream);
   if (e != cudaSuccess) return e;
   // The dynamic shared-memory opt-in is a per-device function attribute.
   static bool attr_set[64] = {};
@@ -1026,9 +1018,7 @@ cudaError_t prefill_setup(const PrefillParams& p, cudaStream_t stream, CUtensorM
   e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    e = cudaFuncSetAttribute(prefill_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmAlloc);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(prefill_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmAlloc);
+    e = cudaFuncSetAttribute(prefill_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmAlloc);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
@@ -1068,15 +1058,20 @@ cudaError_t launch_prefill_state_map(const PrefillParams& p, cudaStream_t stream
   CUtensorMap mk, mq, mv, mo;
   cudaError_t e = prefill_setup(q, stream, &mk, &mq, &mv, &mo);
   if (e != cudaSuccess) return e;
-  chain_kernel_for(q)<<<dim3(p.HV, p.N, 2 * S), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2 * S), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
   e = cudaGetLastError();
   if (e != cudaSuccess || S == 1) return e;
   map_combine_kernel<<<dim3(p.HV, p.N, 8), 256, 0, stream>>>(q);
   return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream) {
-  if (p.N == 0) return cudaSuccess;
+cudaError_t launch_prefill_chunk(const PrefillParams& p_in, cudaStream_t stream) {
+  if (p_in.N == 0) return cudaSuccess;
+  PrefillParams p = p_in;
+  if (p.flags & kFlagQkL2Norm) {
+    const size_t base = chunk_records_and_cp_bytes(p.N, p.T, p.HV, p.flags);
+    p.qnorm = reinterpret_cast<float2*>(static_cast<unsigned char*>(p.workspace) + ((base + 255) & ~(size_t)255));
+  }
   CUtensorMap mk, mq, mv, mo;
   cudaError_t e = prefill_setup(p, stream, &mk, &mq, &mv, &mo);
   if (e != cudaSuccess) return e;
@@ -1085,7 +1080,7 @@ cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream) {
     PrefillParams q = p;
     q.cp_segments = 1;
     q.cp_pass = 0;
-    chain_kernel_for(q)<<<dim3(p.HV, p.N), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+    prefill_chunk_kernel<<<dim3(p.HV, p.N), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
     return cudaGetLastError();
   }
   // context parallelism: segment maps, their composition, the segment reruns
@@ -1094,13 +1089,13 @@ cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream) {
   q.cp_segments = S;
   q.cp_scratch = reinterpret_cast<float*>(static_cast<unsigned char*>(p.workspace) + ((records + 255) & ~(size_t)255));
   q.cp_pass = 1;
-  chain_kernel_for(q)<<<dim3(p.HV, p.N, S >= 3 ? 2 * S - 3 : 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, S >= 3 ? 2 * S - 3 : 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   e = launch_prefill_combine(q, stream);
   if (e != cudaSuccess) return e;
   q.cp_pass = 3;
-  chain_kernel_for(q)<<<dim3(p.HV, p.N, S - 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, S - 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
   return cudaGetLastError();
 }
 

@@ -40,45 +40,25 @@ constexpr uint32_t kRecGates = 1792;   // 7 x 64 fp32
 constexpr uint32_t kRecBytes = kRecT + kRecGates;
 static_assert(kRecBytes % 16 == 0, "record alignment");
 
-// gate arrays (per chunk, 64 tokens each), with n_t = 1 / |k_t| when q and k are
-// L2-normalised in the kernel (GDN_FLAG_QK_L2NORM) and n_t = 1 otherwise:
-//   GA_G2   log2-scaled decay prefix g2_t = log2 e * sum_{i<=t} log g_i
+// gate arrays (per chunk, 64 tokens each), with n_t = 1 / |k_t| and m_t = 1 / |q_t| when q
+// and k are L2-normalised in the kernels (GDN_FLAG_QK_L2NORM), n_t = m_t = 1 otherwise:
+//   GA_G2   g2_t + log2 m_t, g2_t = log2 e * sum_{i<=t} log g_i the log2-scaled decay prefix
+//           (row term of the decayed Q K^T product)
 //   GA_BETA beta_t
-//   GA_G    G_t = exp(g_t)
+//   GA_G    G_t m_t, G_t = exp(g_t) (scales column t of S0 Q^T)
 //   GA_BG   beta_t G_t n_t
 //   GA_R    exp(g_C - g_t) n_t (the decay to the chunk end)
 //   GA_G2C  g2_t - log2 n_t (column term of the decayed K K^T and Q K^T products)
 //   GA_GC   G_C = exp(g_C) in every entry
-// The normalisation of k_t is folded into these per-token factors (k stays raw bf16 in
-// every product); that of q_t (m_t = 1 / |q_t|) is applied by the chain kernel, which
-// holds the Q tiles.  Tokens past the sequence end carry beta = 0, log g = 0 (the prefix
-// stays flat) and n = 1, so they change nothing.
+// The normalisation is folded into these per-token factors: q and k stay raw bf16 in
+// every product, so the chain kernel is the same with and without it.  Tokens past the
+// sequence end carry beta = 0, log g = 0 (the prefix stays flat) and n = m = 1, so they
+// change nothing.
 enum : int { GA_G2 = 0, GA_BETA = 1, GA_G = 2, GA_BG = 3, GA_R = 4, GA_G2C = 5, GA_GC = 6, GA_N = 7 };
 
 // 1 / sqrt(sum of squares + eps): the L2 normalisation factor (eps 1e-6, as the decode and
 // token-serial kernels use).
 __device__ __forceinline__ float l2_factor(float sumsq) { return rsqrtf(sumsq + 1e-6f); }
-
-// Sum of squares of row `r` of a 128-feature bf16 row set held as two SW128 tiles
-// (features 0-63 at tile0, 64-127 at tile0 + tile_stride).
-__device__ __forceinline__ float row_sumsq(const unsigned char* tile0, uint32_t tile_stride, int r) {
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-  for (int f = 0; f < 2; ++f) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint4 w = *reinterpret_cast<const uint4*>(tile0 + f * tile_stride + r * 128 + ((c ^ (r & 7)) << 4));
-      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float lo = __uint_as_float(u[e] << 16), hi = __uint_as_float(u[e] & 0xffff0000u);
-        s0 = fmaf(lo, lo, s0);
-        s1 = fmaf(hi, hi, s1);
-      }
-    }
-  }
-  return s0 + s1;
-}
 
 __host__ __device__ inline int64_t num_slots(int64_t total_tokens, int num_seqs) {
   return total_tokens / kC + num_seqs + 1;
@@ -154,5 +134,7 @@ __device__ __forceinline__ void token_gates(float eA, float dt_bias, float a, fl
 // kernel's K tensor map, 64-token x 64-feature SW128 boxes).
 cudaError_t launch_prefill_combine(const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_prefill_prep(const PrefillParams& p, const CUtensorMap& mapK, cudaStream_t stream);
+// 1 / |q| and log2 (1 / |q|) of every (token, q/k head) into p.qnorm (GDN_FLAG_QK_L2NORM).
+cudaError_t launch_qk_norm(const PrefillParams& p, cudaStream_t stream);
 
 }  // namespace gdn

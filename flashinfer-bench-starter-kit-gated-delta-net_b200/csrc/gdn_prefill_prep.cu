@@ -43,7 +43,11 @@ constexpr uint32_t kKTile = 16384;
 constexpr uint32_t kSmAT = 0;
 constexpr uint32_t kATBytes = 64 * kLd * 4;
 constexpr uint32_t kSmGate = kSmAT + 2 * kATBytes;  // per group: GA_N x 64 fp32 + scan scratch
-constexpr uint32_t kGateBytes = (GA_N + 2) * 64 * 4;  // GA_N arrays + scan scratch + n_t
+// per group, 64 fp32 each: g2_t, beta_t, G_t, g2_C (log2 e g_C), log2 m_t, m_t (q
+// normalisation), scan scratch, then (after the K K^T diagonal) n_t and log2 n_t (k
+// normalisation), the column term g2_t - log2 n_t and the row factor beta_t n_t of A
+enum : int { PG_G2 = 0, PG_BETA, PG_G, PG_GC2, PG_LM, PG_M, PG_SCAN, PG_N, PG_LN, PG_G2C, PG_BN, PG_COUNT };
+constexpr uint32_t kGateBytes = PG_COUNT * 64 * 4;
 constexpr uint32_t kSmBar = kSmGate + 2 * kGateBytes;
 constexpr uint32_t kSmMisc = kSmBar + 16;  // tmem base slot, per-group chunk info
 constexpr uint32_t kSmBytes = kSmMisc + 80;
@@ -286,52 +290,43 @@ __global__ void __launch_bounds__(kThreads, 4)
   float* AT = reinterpret_cast<float*>(base + kSmAT + grp * kATBytes);
   float* gates = reinterpret_cast<float*>(base + kSmGate + grp * kGateBytes);
   unsigned char* rec = mine.nvalid ? record(p, mine.slot, h) : nullptr;
-  // ---- gates (threads 0-63 of the group, token t = gth) ----
+  const bool l2norm = (p.flags & kFlagQkL2Norm) != 0;
+  // ---- gates (threads 0-63 of the group, token t = gth); with the q/k L2 norm also the
+  //      token's q norm (computed once per token and q/k head by qk_norm_kernel) ----
   if (mine.nvalid && gth < 64) {
-    {
-      const float eA = tc::ex2_approx(p.A_log[h] * kLog2e), dt_bias = p.dt_bias[h];
-      float lg = 0.f, bt = 0.f;
-      if (gth < mine.nvalid) {
-        const int64_t tok = mine.z + gth;
-        const float a = __bfloat162float(p.a[tok * p.a_st + h]);
-        const float b = __bfloat162float(p.b[tok * p.b_st + h]);
-        token_gates(eA, dt_bias, a, b, lg, bt);
+    const float eA = tc::ex2_approx(p.A_log[h] * kLog2e), dt_bias = p.dt_bias[h];
+    float lg = 0.f, bt = 0.f, lm = 0.f, m = 1.f;
+    if (gth < mine.nvalid) {
+      const int64_t tok = mine.z + gth;
+      const float a = __bfloat162float(p.a[tok * p.a_st + h]);
+      const float b = __bfloat162float(p.b[tok * p.b_st + h]);
+      if (l2norm) {  // m_t = 1 / |q_t| and its log2
+        const float2 mq = p.qnorm[tok * p.HQ + h / p.ratio];
+        m = mq.x;
+        lm = mq.y;
       }
-      float x = lg;  // inclusive scan over the 64 tokens: warp scans + carry
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-      }
-      float* tmp = gates + GA_N * 64;
-      if (gth == 31) tmp[0] = x;
-      named_sync(bar64, 64);
-      if (gth >= 32) x += tmp[0];
-      if (gth == 63) tmp[1] = x;
-      named_sync(bar64, 64);
-      // k normalisation (GDN_FLAG_QK_L2NORM): n_t = 1 / |k_t| from the chunk's K rows in
-      // shared memory, once they have landed
-      float nk = 1.f, lg2n = 0.f;
-      if ((p.flags & kFlagQkL2Norm) && mbar_wait_sleep(bar_tma, 0) && gth < mine.nvalid) {
-        const float ss = row_sumsq(base + kSmK + grp * 8192, kKTile, gth);
-        nk = l2_factor(ss);
-        lg2n = -0.5f * tc::lg2_approx(ss + 1e-6f);
-      }
-      const float x2 = x * kLog2e, gC2 = tmp[1] * kLog2e;
-      const float G = tc::ex2_approx(x2), GC = tc::ex2_approx(gC2);
-      const float vals[GA_N] = {x2, bt, G, bt * G * nk, tc::ex2_approx(gC2 - x2) * nk, x2 - lg2n, GC};
-      float* rg = reinterpret_cast<float*>(rec + kRecT);
-#pragma unroll
-      for (int a = 0; a < GA_N; ++a) {
-        gates[a * 64 + gth] = vals[a];
-        rg[a * 64 + gth] = vals[a];
-      }
-      gates[(GA_N + 1) * 64 + gth] = bt * nk;  // row factor of A
+      token_gates(eA, dt_bias, a, b, lg, bt);
     }
+    float x = lg;  // inclusive scan over the 64 tokens: warp scans + carry
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    float* tmp = gates + PG_SCAN * 64;
+    if (gth == 31) tmp[0] = x;
+    named_sync(bar64, 64);
+    if (gth >= 32) x += tmp[0];
+    if (gth == 63) tmp[1] = x;
+    named_sync(bar64, 64);
+    const float x2 = x * kLog2e, gC2 = tmp[1] * kLog2e;
+    gates[PG_G2 * 64 + gth] = x2;
+    gates[PG_BETA * 64 + gth] = bt;
+    gates[PG_G * 64 + gth] = tc::ex2_approx(x2);
+    gates[PG_GC2 * 64 + gth] = gC2;
+    gates[PG_LM * 64 + gth] = lm;
+    gates[PG_M * 64 + gth] = m;
   }
-  // the K tiles are read for the k norms by both groups before either group's A / T array
-  // overlays them
-  if (p.flags & kFlagQkL2Norm) __syncthreads();
   if (mine.nvalid) {
     named_sync(bar128, 128);
     // ---- A rows from TMEM (the two warps whose lane quarter holds this slot's rows) ----
@@ -347,13 +342,49 @@ __global__ void __launch_bounds__(kThreads, 4)
       ok = all;
     }
     if (ok) {
+      const bool arow = ((warp & 3) >> 1) == grp;  // this warp's lane quarter holds slot rows
+      const int t_row = ((warp & 1) << 5) | lane;
+      const uint32_t d0 = tc::tmem_addr(tmem, (uint32_t)((warp & 3) * 32), (uint32_t)(grp * 64));
       tc::fence_after_sync();
-      if (((warp & 3) >> 1) == grp) {
-        const int t = ((warp & 1) << 5) | lane;
+      // k normalisation: n_t = 1 / |k_t| from the diagonal of K K^T (row t, column t)
+      if (l2norm && arow) {
+        float diag = 0.f;
+        const int c0 = (warp & 1) * 4;  // the warp's rows are columns 8 c0 .. 8 c0 + 31
+#pragma unroll
+        for (int g4 = 0; g4 < 4; ++g4) {
+          float v[8];
+          tc::tmem_ld8(d0 + (c0 + g4) * 8, v);
+          tc::tmem_wait_ld();
+          if ((t_row >> 3) == c0 + g4) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if ((t_row & 7) == u) diag = v[u];
+          }
+        }
+        gates[PG_N * 64 + t_row] = t_row < mine.nvalid ? l2_factor(diag) : 1.f;
+        gates[PG_LN * 64 + t_row] = t_row < mine.nvalid ? -0.5f * tc::lg2_approx(diag + 1e-6f) : 0.f;
+      }
+      named_sync(bar128, 128);
+      // ---- the chunk's gate arrays (record) and A's column term and row factor ----
+      if (gth < 64) {
+        const float n = l2norm ? gates[PG_N * 64 + gth] : 1.f;
+        const float ln = l2norm ? gates[PG_LN * 64 + gth] : 0.f;  // log2 n_t
+        const float x2 = gates[PG_G2 * 64 + gth], bt = gates[PG_BETA * 64 + gth], G = gates[PG_G * 64 + gth];
+        const float gC2 = gates[PG_GC2 * 64 + gth], m = gates[PG_M * 64 + gth], lm = gates[PG_LM * 64 + gth];
+        const float r = tc::ex2_approx(gC2 - x2);  // exp(g_C - g_t)
+        const float vals[GA_N] = {x2 + lm, bt, G * m, bt * G * n, r * n, x2 - ln, tc::ex2_approx(gC2)};
+        float* rg = reinterpret_cast<float*>(rec + kRecT);
+#pragma unroll
+        for (int a = 0; a < GA_N; ++a) rg[a * 64 + gth] = vals[a];
+        gates[PG_G2C * 64 + gth] = x2 - ln;
+        gates[PG_BN * 64 + gth] = bt * n;
+      }
+      named_sync(bar128, 128);
+      if (arow) {
+        const int t = t_row;
         // A[t][j] = beta_t n_t exp2(g2_t - (g2_j - log2 n_j)) (k_t.k_j) = beta_t exp(g_t - g_j) k^_t.k^_j
-        const float* g2 = gates + GA_G2C * 64;
-        const float gt = gates[GA_G2 * 64 + t], bt = gates[(GA_N + 1) * 64 + t];
-        const uint32_t d0 = tc::tmem_addr(tmem, (uint32_t)((warp & 3) * 32), (uint32_t)(grp * 64));
+        const float* g2 = gates + PG_G2C * 64;
+        const float gt = gates[PG_G2 * 64 + t], bt = gates[PG_BN * 64 + t];
 #pragma unroll 2
         for (int j8 = 0; j8 < 8; ++j8) {
           float v[8];
@@ -411,7 +442,53 @@ __global__ void __launch_bounds__(kThreads, 4)
   }
 }
 
+// 1 / |q| and its log2 for every (token, q/k head): a streaming pass over q, 16 lanes per
+// 256-byte row (coalesced 16-byte loads), 8 rows per warp per iteration.
+__global__ void __launch_bounds__(256) qk_norm_kernel(PrefillParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = p.T * (int64_t)p.HQ;
+  const int64_t nwarps = (int64_t)gridDim.x * 8;
+  for (int64_t r0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * 8; r0 < rows; r0 += nwarps * 8) {
+    float ss[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = r0 + 2 * i + (lane >> 4);
+      ss[i] = 0.f;
+      if (row < rows) {
+        const int64_t tok = row / p.HQ;
+        const int hq = (int)(row - tok * p.HQ);
+        const uint4 w = *reinterpret_cast<const uint4*>(p.q + tok * p.q_st + (int64_t)hq * p.q_sh + (lane & 15) * 8);
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = __uint_as_float(u[e] << 16), hi = __uint_as_float(u[e] & 0xffff0000u);
+          ss[i] = fmaf(lo, lo, fmaf(hi, hi, ss[i]));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], o);
+    if ((lane & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t row = r0 + 2 * i + (lane >> 4);
+        if (row < rows) p.qnorm[row] = make_float2(l2_factor(ss[i]), -0.5f * tc::lg2_approx(ss[i] + 1e-6f));
+      }
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_qk_norm(const PrefillParams& p, cudaStream_t stream) {
+  const int64_t rows = p.T * (int64_t)p.HQ;
+  if (rows <= 0) return cudaSuccess;
+  const int64_t blocks = (rows + 63) / 64;
+  qk_norm_kernel<<<(unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_prefill_prep(const PrefillParams& p, const CUtensorMap& mapK, cudaStream_t stream) {
   const int64_t slots = num_slots(p.T, p.N);

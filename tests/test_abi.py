@@ -93,13 +93,15 @@ def test_prefill_rejects_bad_arguments(lib):
 
 def test_workspace_size(lib):
     """One 18,176-byte record (T hi/lo tiles + 7 gate arrays) per chunk slot and
-    v-head; slots = total_tokens // 64 + num_seqs + 1, with or without in-kernel q/k
-    normalisation.  The forced token-serial path needs no workspace."""
+    v-head; slots = total_tokens // 64 + num_seqs + 1.  In-kernel q/k normalisation
+    adds one (1/|q|, log2 1/|q|) float pair per token and v-head after the records,
+    256-byte aligned.  The forced token-serial path needs no workspace."""
     a = lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
     assert a == lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
     assert a == (34000 // 64 + 16 + 1) * 32 * 18176
     assert lib.gdn_prefill_workspace_size(8, 8 * 32768, 16, 32, 128, 0) == (4096 + 9) * 32 * 18176
-    assert lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0x1) == a  # GDN_FLAG_QK_L2NORM
+    # GDN_FLAG_QK_L2NORM
+    assert lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0x1) == ((a + 255) & ~255) + 34000 * 32 * 8
     assert lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0x2) == 0  # GDN_FLAG_PREFILL_SERIAL
     assert lib.gdn_prefill_workspace_size(0, 0, 16, 32, 128, 0) == 0
 
