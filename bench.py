@@ -751,7 +751,7 @@ def run_ours(args, world, rank, local):
                 "tokens_per_s": sum_over_ranks(mb * mt, world) / (mms * 1e-3), "ms_per_step": mms, "steps": msteps,
                 "roofline": {"bound": "hbm", "achieved": mbytes / (mlaunch * 1e-3) / 1e9, "peak": hbm_peak,
                              "unit": "GB/s", "frac": mbytes / (mlaunch * 1e-3) / 1e9 / hbm_peak,
-                             "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)", "kernel": "decode_mtp_pipe_kernel",
+                             "peak_kind": f"{peak_kind} hbm_gbs (copy, burst)", "kernel": "decode_mtp_chunk_kernel",
                              "traffic": profile_traffic("gdn_decode_mtp_b64_t4"),
                              "avg_launch_us": mlaunch * 1e3, "algorithmic_bytes_per_launch": mbytes},
                 "clocks": sampler_m.summary()}

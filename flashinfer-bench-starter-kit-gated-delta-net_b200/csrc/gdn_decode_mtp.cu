@@ -548,12 +548,429 @@ __global__ void __launch_bounds__(kPipeWarps * 32, 4) decode_mtp_pipe_kernel(Dec
   }
 }
 
+// ---------------------------------------------------------------------------
+// Chunked multi-token kernel (2 <= T <= kChunkMaxT tokens, no intermediate states,
+// q/k/v rows 16-byte aligned): every token's dot products with the state come
+// from the item's initial rows at once instead of one token after another.
+//
+// For one state row s and tokens t = 0 .. T-1 the decode recurrence is
+//   s_t = g_t s_{t-1} + d_t k_t,   d_t = beta_t (v_t - g_t s_{t-1}.k_t),
+//   o_t = scale (g_t s_{t-1}.q_t + d_t k_t.q_t).
+// Every dot product of a later state with a token vector w follows from the
+// products with the initial row and the Gram scalars of the token vectors:
+//   z_t(w) = s_t.w = g_t z_{t-1}(w) + d_t (k_t.w),   z_{-1}(w) = s.w,
+// and the final row is s_{T-1} = (prod_t g_t) s + sum_j c_j k_j with
+// c_j = d_j prod_{i>j} g_i.  Per unit of 16 rows of one (sequence, v-head), the
+// token rows, gates and (G) once, then (A)-(C) for each 8-row half:
+//   A  the 2T products s.k_t, s.q_t of each row, all independent, reduced
+//      together over the row's 8 lanes (the only products with the state);
+//   G  the T^2 Gram scalars k_j.k_t (j < t) and k_j.q_t (j <= t) (+ |k_t|^2 and
+//      |q_t|^2 for the in-kernel L2 norm), each lane over 4 of the 128
+//      features, reduce-scattered over the warp into shared memory;
+//   B  the recurrence on scalars per row (z, d_t, o_t, c_j);
+//   C  one pass over the row: s <- (prod g) s + sum_j c_j k_j.
+// Against the token-serial form this takes one reduction round per row pair
+// instead of one per token and one multiply-add per token and element in the
+// state update, and no token waits for the previous one.  The state still
+// crosses HBM once per call; each unit's rows and token rows are bulk-copied
+// one unit ahead (one stage each: the tokens are widened to fp32 at the start of
+// the unit and the rows move to registers half by half, which frees the buffers).
+constexpr int kChunkMaxT = 4;
+constexpr int kChunkWarps = 4;
+
+// Enumeration of the Gram scalars of T tokens (vectors w < T are k_w, w >= T are
+// q_{w - T}): token t owns kk(j, t) = k_j.k_t for j < t, then kq(j, t) = k_j.q_t
+// for j <= t (2 t + 1 scalars from index t^2); then |k_t|^2, |q_t|^2.
+template <int T, bool L2NORM>
+struct ChunkGram {
+  static constexpr int kDots = T * T + (L2NORM ? 2 * T : 0);
+  static constexpr int kPad = kDots <= 1 ? 1 : kDots <= 2 ? 2 : kDots <= 4 ? 4 : kDots <= 8 ? 8 : kDots <= 16 ? 16 : 32;
+  static_assert(kDots <= 32, "Gram scalars of at most 32");
+  static constexpr int kk(int j, int t) { return t * t + j; }
+  static constexpr int kq(int j, int t) { return t * t + t + j; }
+  static constexpr int nk(int t) { return T * T + t; }
+  static constexpr int nq(int t) { return T * T + T + t; }
+  static constexpr int va(int d) {  // first vector of scalar d
+    for (int t = 0; t < T; ++t) {
+      if (d < t * t + t) return d - t * t;
+      if (d < t * t + 2 * t + 1) return d - t * t - t;
+    }
+    return d < T * T + T ? d - T * T : T + (d - T * T - T);
+  }
+  static constexpr int vb(int d) {  // second vector of scalar d
+    for (int t = 0; t < T; ++t) {
+      if (d < t * t + t) return t;
+      if (d < t * t + 2 * t + 1) return T + t;
+    }
+    return d < T * T + T ? d - T * T : T + (d - T * T - T);
+  }
+  static constexpr uint32_t kBytes = (uint32_t)((kPad * 4 + 15) / 16 * 16);
+};
+
+// Reduce-scatter of N (a power of two) per-lane partial sums over the warp: after
+// it, for N >= 32 lane l holds the full sums of scalars l N/32 .. l N/32 + N/32 - 1
+// in v[0 ..]; for N < 32 it holds scalar l >> (5 - log2 N) in v[0].
+template <int N, int M>
+struct WarpReduceScatter {
+  __device__ __forceinline__ static void run(float* v, int lane) {
+    if constexpr (M > 0) {
+      if constexpr (N > 1) {
+        constexpr int H = N / 2;
+        const bool up = (lane & M) != 0;
+#pragma unroll
+        for (int i = 0; i < H; ++i) {
+          const float send = up ? v[i] : v[i + H];
+          const float keep = up ? v[i + H] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, M);
+        }
+        WarpReduceScatter<H, M / 2>::run(v, lane);
+      } else {
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], M);
+        WarpReduceScatter<1, M / 2>::run(v, lane);
+      }
+    }
+  }
+};
+
+constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n / 2); }
+
+// Work unit of the chunked kernel: 16 consecutive state rows of one (sequence, v-head),
+// processed as two 8-row halves; the token rows, the gates and the Gram scalars are
+// prepared once per unit and serve both halves.
+constexpr int kChunkRows = 16;
+constexpr uint32_t kChunkRowBytes = kChunkRows * kHeadDim * 4;  // 8192
+// token rows of a unit: q and k (256 B each) per token, then v of the unit's 16 rows (32 B) per token
+__host__ __device__ constexpr uint32_t chunk_tok_bytes(int T) { return (uint32_t)T * (2 * kHeadDim * 2 + kChunkRows * 2); }
+// per token in shared memory: v of the 16 rows, g, beta (fp32)
+constexpr int kChunkScal = kChunkRows + 2;
+
+template <int T, bool L2NORM>
+__host__ __device__ constexpr uint32_t chunk_warp_bytes() {
+  // rows [16][128] fp32 | token rows | q, k widened [2T][128] fp32 | Gram scalars | per-token scalars |
+  // 2 mbarriers
+  return kChunkRowBytes + chunk_tok_bytes(T) + 2u * T * kHeadDim * 4 + ChunkGram<T, L2NORM>::kBytes +
+         (uint32_t)((T * kChunkScal * 4 + 15) / 16 * 16) + 16;
+}
+
+// unit u = (b * HV + h) * 8 + row block of 16 (the division by HV as in pipe_item)
+__device__ __forceinline__ PipeItem chunk_unit(int u, const DecodeMtpParams& p) {
+  PipeItem it;
+  it.wrow0 = (u & (kHeadDim / kChunkRows - 1)) * kChunkRows;
+  const uint32_t bh = (uint32_t)u >> 3;
+  it.bi = (int)((__umulhi(bh, p.hv_mul) + bh) >> p.hv_shr);
+  it.h = (int)bh - it.bi * p.HV;
+  return it;
+}
+static_assert(kHeadDim / kChunkRows == 8, "8 row blocks per head");
+
+template <int T, bool L2NORM>
+__global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(DecodeMtpParams p) {
+  using G = ChunkGram<T, L2NORM>;
+  constexpr uint32_t kTok = chunk_tok_bytes(T);
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned char* wbase = smem_raw + (size_t)warp * chunk_warp_bytes<T, L2NORM>();
+  float* rows_buf = reinterpret_cast<float*>(wbase);
+  unsigned char* tok_buf = wbase + kChunkRowBytes;
+  float* qk32 = reinterpret_cast<float*>(tok_buf + kTok);  // [2T][128]: k_0 .. k_{T-1}, q_0 .. q_{T-1}
+  float* gram = qk32 + 2 * T * kHeadDim;
+  float* scal = gram + G::kBytes / 4;  // [T][kChunkScal]: v of rows 0-15, g, beta
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      reinterpret_cast<unsigned char*>(scal) + (T * kChunkScal * 4 + 15) / 16 * 16);  // rows, tokens
+
+  const int n_units = p.B * p.HV * (kHeadDim / kChunkRows);  // < 2^31 (checked by the launcher)
+  const int first = blockIdx.x * kChunkWarps + warp, step = gridDim.x * kChunkWarps;
+  if (first >= n_units) return;
+  const int rg = lane >> 3, cs = lane & 7;
+
+  if (lane == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  auto issue_rows = [&](const PipeItem& it, int64_t slot) {
+    if (lane == 0) {
+      if (slot >= 0 && slot < p.P) {
+        mbar_arrive_expect_tx(&bars[0], kChunkRowBytes);
+        bulk_g2s_evict_first(rows_buf,
+                             p.pool + (size_t)slot * p.s_sn + (size_t)it.h * p.s_sh + (size_t)it.wrow0 * kHeadDim,
+                             kChunkRowBytes, &bars[0]);
+      } else {
+        mbar_arrive(&bars[0]);  // nothing to load: complete the phase
+      }
+    }
+  };
+  auto issue_tok = [&](const PipeItem& it) {
+    if (lane == 0) mbar_arrive_expect_tx(&bars[1], kTok);
+    __syncwarp();
+    const int qh = it.h / p.ratio;
+    if (lane < T) {
+      bulk_g2s(tok_buf + lane * 512, p.q + (size_t)it.bi * p.q_sb + (size_t)lane * p.q_st + (size_t)qh * p.q_sh, 256,
+               &bars[1]);
+    } else if (lane < 2 * T) {
+      const int t = lane - T;
+      bulk_g2s(tok_buf + t * 512 + 256, p.k + (size_t)it.bi * p.k_sb + (size_t)t * p.k_st + (size_t)qh * p.k_sh, 256,
+               &bars[1]);
+    } else if (lane < 3 * T) {
+      const int t = lane - 2 * T;
+      bulk_g2s(tok_buf + T * 512 + t * 32,
+               p.v + (size_t)it.bi * p.v_sb + (size_t)t * p.v_st + (size_t)it.h * p.v_sh + it.wrow0, 32, &bars[1]);
+    }
+  };
+  auto load_gate_inputs = [&](const PipeItem& it, bool have, float& ga, float& gb, float& alog, float& dtb) {
+    ga = gb = alog = dtb = 0.f;
+    if (have && lane < T) {
+      ga = bf16_to_f32(p.a + (size_t)it.bi * p.a_sb + (size_t)lane * p.a_st + it.h);
+      gb = bf16_to_f32(p.b + (size_t)it.bi * p.b_sb + (size_t)lane * p.b_st + it.h);
+      alog = p.A_log[it.h];
+      dtb = p.dt_bias[it.h];
+    }
+  };
+
+  // prologue: the first unit's rows and tokens in flight, the next unit's pool index
+  PipeItem cur = chunk_unit(first, p), nx = chunk_unit(first + step < n_units ? first + step : first, p);
+  int64_t slot_cur = load_index(p, cur.bi);
+  int64_t slot_next = first + step < n_units ? load_index(p, nx.bi) : -1;
+  issue_rows(cur, slot_cur);
+  issue_tok(cur);
+  uint32_t rows_issued = 1, rows_done = 0, tok_issued = 1, tok_done = 0;  // per barrier: phases armed / waited
+  float ga, gb, alog, dtb;
+  load_gate_inputs(cur, true, ga, gb, alog, dtb);
+
+  bool fail = false;
+  for (int u = first; u < n_units; u += step) {
+    const PipeItem it = cur;
+    const int64_t slot = slot_cur;
+    const bool valid = slot >= 0 && slot < p.P;
+    const bool more = u + step < n_units;
+    // this unit's gates (lane t: token t), then the next unit's inputs and the pool index after it
+    float g_l = 0.f, beta_l = 0.f;
+    if (lane < T) gdn_gates(alog, ga, dtb, gb, g_l, beta_l);
+    load_gate_inputs(nx, more, ga, gb, alog, dtb);
+    const bool more2 = u + 2 * step < n_units;
+    const PipeItem nn = chunk_unit(more2 ? u + 2 * step : u, p);
+    const int64_t slot_nn = more2 ? load_index(p, nn.bi) : -1;
+
+    // ---- tokens: q and k widened to fp32 (lane: features 4 lane .. 4 lane + 3 of every
+    //      vector), the Gram partials from the same registers, v and gates as fp32 ----
+    if (!mbar_wait(&bars[1], tok_done & 1)) { fail = true; break; }
+    ++tok_done;
+    float4 wv[2 * T];
+#pragma unroll
+    for (int w = 0; w < 2 * T; ++w) {
+      const int t = w < T ? w : w - T;
+      const uint2 r = *reinterpret_cast<const uint2*>(tok_buf + t * 512 + (w < T ? 256 : 0) + lane * 8);
+      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+      wv[w] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      *reinterpret_cast<float4*>(qk32 + w * kHeadDim + lane * 4) = wv[w];
+    }
+    {
+      const __nv_bfloat16* vt = reinterpret_cast<const __nv_bfloat16*>(tok_buf + T * 512);
+#pragma unroll
+      for (int e = lane; e < kChunkRows * T; e += 32)  // token e / 16, row e % 16
+        scal[(e >> 4) * kChunkScal + (e & 15)] = __bfloat162float(vt[e]);
+    }
+    if (lane < T) {
+      scal[lane * kChunkScal + kChunkRows] = g_l;
+      scal[lane * kChunkScal + kChunkRows + 1] = beta_l;
+    }
+    __syncwarp();  // the token buffer is read; every lane's q, k features are in qk32
+    if (more) {
+      issue_tok(nx);
+      ++tok_issued;
+    }
+    {
+      float gp[G::kPad];
+#pragma unroll
+      for (int d = 0; d < G::kPad; ++d) {
+        if (d < G::kDots) {
+          const float4 x = wv[G::va(d)], y = wv[G::vb(d)];
+          gp[d] = fmaf(x.x, y.x, fmaf(x.y, y.y, fmaf(x.z, y.z, x.w * y.w)));
+        } else {
+          gp[d] = 0.f;
+        }
+      }
+      WarpReduceScatter<G::kPad, 16>::run(gp, lane);
+      if constexpr (G::kPad >= 32) {
+#pragma unroll
+        for (int i = 0; i < G::kPad / 32; ++i) gram[lane * (G::kPad / 32) + i] = gp[i];
+      } else {
+        constexpr int sh = 5 - ilog2(G::kPad);
+        if ((lane & ((1 << sh) - 1)) == 0) gram[lane >> sh] = gp[0];
+      }
+    }
+    if (!mbar_wait(&bars[0], rows_done & 1)) { fail = true; break; }
+    ++rows_done;
+    __syncwarp();  // Gram scalars written
+    float nkv[T], nqv[T];  // 1 / |k_t|, 1 / |q_t| with the L2 norm, else 1
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      nkv[t] = L2NORM ? rsqrtf(gram[G::nk(t)] + 1e-6f) : 1.f;
+      nqv[t] = L2NORM ? rsqrtf(gram[G::nq(t)] + 1e-6f) : 1.f;
+    }
+
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      // ---- this half's 8 rows -> registers (after the second half the rows buffer is free) ----
+      float2 s[2][8];
+      if (valid) {
+#pragma unroll
+        for (int ps = 0; ps < 2; ++ps) {
+          const float* src = rows_buf + (half * 8 + ps * 4 + rg) * kHeadDim + cs * 4;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            const float4 x = *reinterpret_cast<const float4*>(src + c4 * 32);
+            s[ps][2 * c4] = make_float2(x.x, x.y);
+            s[ps][2 * c4 + 1] = make_float2(x.z, x.w);
+          }
+        }
+      }
+      if (half == 1) {
+        __syncwarp();
+        if (more) {
+          issue_rows(nx, slot_next);
+          ++rows_issued;
+        }
+      }
+      const int r0 = it.wrow0 + half * 8;
+      __nv_bfloat16* out_half = p.out + (size_t)it.bi * p.o_sb + (size_t)it.h * p.o_sh + r0;
+      if (!valid) {
+        if (half == 0 && slot >= p.P && lane == 0) raise_device_error(kDevErrBadIndex);
+        for (int e = lane; e < T * 8; e += 32)
+          out_half[(size_t)(e >> 3) * p.o_st + (e & 7)] = __float2bfloat16_rn(0.f);
+        continue;
+      }
+      // ---- A: s.k_t and s.q_t of both rows, each reduced over the row's 8 lanes ----
+      float x[2][2 * T];
+#pragma unroll
+      for (int w = 0; w < 2 * T; ++w) {
+        float2 a0 = make_float2(0.f, 0.f), a1 = a0;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          const float4 f = *reinterpret_cast<const float4*>(qk32 + w * kHeadDim + c4 * 32 + cs * 4);
+          const float2 lo = make_float2(f.x, f.y), hi = make_float2(f.z, f.w);
+          a0 = __ffma2_rn(s[0][2 * c4], lo, a0);
+          a1 = __ffma2_rn(s[1][2 * c4], lo, a1);
+          a0 = __ffma2_rn(s[0][2 * c4 + 1], hi, a0);
+          a1 = __ffma2_rn(s[1][2 * c4 + 1], hi, a1);
+        }
+        float2 r = __fadd2_rn(make_float2(a0.x, a1.x), make_float2(a0.y, a1.y));
+#pragma unroll
+        for (int m = 1; m < 8; m <<= 1)
+          r = __fadd2_rn(r, make_float2(__shfl_xor_sync(0xffffffffu, r.x, m), __shfl_xor_sync(0xffffffffu, r.y, m)));
+        x[0][w] = r.x;
+        x[1][w] = r.y;
+      }
+      // ---- B: the token recurrence on scalars ----
+      const float scale = p.scale;
+      float om[2], cc[2][T];  // om: the output of token cs (this lane's store)
+#pragma unroll
+      for (int ps = 0; ps < 2; ++ps) {
+        float z[2 * T];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          z[t] = x[ps][t] * nkv[t];
+          z[T + t] = x[ps][T + t] * nqv[t];
+        }
+        float dl[T];
+        om[ps] = 0.f;
+        const int vr = half * 8 + ps * 4 + rg;
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float g = scal[t * kChunkScal + kChunkRows];
+          const float d = scal[t * kChunkScal + kChunkRows + 1] * (scal[t * kChunkScal + vr] - g * z[t]);
+          const float o = scale * fmaf(d, gram[G::kq(t, t)] * (nkv[t] * nqv[t]), g * z[T + t]);
+          om[ps] = cs == t ? o : om[ps];
+          dl[t] = d;
+#pragma unroll
+          for (int t2 = t + 1; t2 < T; ++t2) {
+            z[t2] = fmaf(d, gram[G::kk(t, t2)] * (nkv[t] * nkv[t2]), g * z[t2]);
+            z[T + t2] = fmaf(d, gram[G::kq(t, t2)] * (nkv[t] * nqv[t2]), g * z[T + t2]);
+          }
+        }
+        float tail = 1.f;  // prod_{i > j} g_i
+#pragma unroll
+        for (int t = T - 1; t >= 0; --t) {
+          cc[ps][t] = dl[t] * tail * nkv[t];
+          tail *= scal[t * kChunkScal + kChunkRows];
+        }
+      }
+      // token cs's outputs of the lane's two rows (lanes cs < T)
+      if (cs < T) {
+        __nv_bfloat16* ot = out_half + (size_t)cs * p.o_st;
+        ot[rg] = __float2bfloat16_rn(om[0]);
+        ot[4 + rg] = __float2bfloat16_rn(om[1]);
+      }
+      // ---- C: s <- (prod g) s + sum_j c_j k_j, then the final rows ----
+      float pg = 1.f;
+#pragma unroll
+      for (int t = 0; t < T; ++t) pg *= scal[t * kChunkScal + kChunkRows];
+      const float2 pg2 = make_float2(pg, pg);
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float2 klo[T], khi[T];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const float4 f = *reinterpret_cast<const float4*>(qk32 + t * kHeadDim + c4 * 32 + cs * 4);
+          klo[t] = make_float2(f.x, f.y);
+          khi[t] = make_float2(f.z, f.w);
+        }
+#pragma unroll
+        for (int ps = 0; ps < 2; ++ps) {
+          float2 lo = __fmul2_rn(s[ps][2 * c4], pg2), hi = __fmul2_rn(s[ps][2 * c4 + 1], pg2);
+#pragma unroll
+          for (int t = 0; t < T; ++t) {
+            const float2 c2 = make_float2(cc[ps][t], cc[ps][t]);
+            lo = __ffma2_rn(c2, klo[t], lo);
+            hi = __ffma2_rn(c2, khi[t], hi);
+          }
+          s[ps][2 * c4] = lo;
+          s[ps][2 * c4 + 1] = hi;
+        }
+      }
+#pragma unroll
+      for (int ps = 0; ps < 2; ++ps) {
+        float* dst = p.new_pool + (size_t)slot * p.n_sn + (size_t)it.h * p.n_sh +
+                     (size_t)(r0 + ps * 4 + rg) * kHeadDim + cs * 4;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+          st_cs_f4(dst + c4 * 32, make_float4(s[ps][2 * c4].x, s[ps][2 * c4].y, s[ps][2 * c4 + 1].x,
+                                              s[ps][2 * c4 + 1].y));
+      }
+    }
+    __syncwarp();  // qk32, the Gram and per-token scalars are read before the next unit overwrites them
+    cur = nx;
+    nx = nn;
+    slot_cur = slot_next;
+    slot_next = slot_nn;
+  }
+  if (fail) {
+    // a copy did not land in time (recorded): wait, bounded, for this warp's copies still
+    // in flight before its shared memory is released
+    if (rows_issued > rows_done && !mbar_wait(&bars[0], rows_done & 1)) return;
+    if (tok_issued > tok_done) mbar_wait(&bars[1], tok_done & 1);
+  }
+}
+
 bool pipe_supported(const DecodeMtpParams& p) {
   if ((long long)p.B * p.HV * (kHeadDim / kPipeRows) >= (1ll << 31)) return false;
   auto al16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
   auto m8 = [](int64_t s) { return (s & 7) == 0; };
   return p.T >= 1 && p.T <= kPipeMaxT && al16(p.q) && al16(p.k) && al16(p.v) && m8(p.q_sb) && m8(p.q_st) &&
          m8(p.q_sh) && m8(p.k_sb) && m8(p.k_st) && m8(p.k_sh) && m8(p.v_sb) && m8(p.v_st) && m8(p.v_sh);
+}
+
+// The item -> (sequence, v-head) divisor of pipe_item for this call's HV.
+DecodeMtpParams with_hv_divisor(const DecodeMtpParams& p) {
+  DecodeMtpParams q = p;
+  int l = 0;
+  while ((1ll << l) < p.HV) ++l;
+  q.hv_shr = l;
+  q.hv_mul = (uint32_t)((((1ull << 32) * ((1ull << l) - (unsigned long long)p.HV)) / (unsigned long long)p.HV) + 1);
+  return q;
 }
 
 template <bool L2NORM>
@@ -581,11 +998,7 @@ cudaError_t launch_pipe(const DecodeMtpParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     occ[dev][p.T] = n > 0 ? n : 1;
   }
-  DecodeMtpParams q = p;
-  int l = 0;
-  while ((1ll << l) < p.HV) ++l;
-  q.hv_shr = l;
-  q.hv_mul = (uint32_t)((((1ull << 32) * ((1ull << l) - (unsigned long long)p.HV)) / (unsigned long long)p.HV) + 1);
+  DecodeMtpParams q = with_hv_divisor(p);
   const long n_items = (long)p.B * p.HV * (kHeadDim / kPipeRows);
   const long need = (n_items + kPipeWarps - 1) / kPipeWarps;
   const long grid = std::min<long>(need, (long)sms[dev] * occ[dev][p.T]);
@@ -593,12 +1006,61 @@ cudaError_t launch_pipe(const DecodeMtpParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+template <int T, bool L2NORM>
+cudaError_t launch_chunk(const DecodeMtpParams& p, cudaStream_t stream) {
+  constexpr size_t smem = (size_t)kChunkWarps * chunk_warp_bytes<T, L2NORM>();
+  // per-device opt-in, SM count and occupancy, looked up once
+  static bool attr_set[64] = {};
+  static int occ[64] = {};
+  static int sms[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    e = cudaFuncSetAttribute(decode_mtp_chunk_kernel<T, L2NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mtp_chunk_kernel<T, L2NORM>, kChunkWarps * 32,
+                                                      smem);
+    if (e != cudaSuccess) return e;
+    occ[dev] = n > 0 ? n : 1;
+    attr_set[dev] = true;
+  }
+  const DecodeMtpParams q = with_hv_divisor(p);
+  const long n_units = (long)p.B * p.HV * (kHeadDim / kChunkRows);
+  const long need = (n_units + kChunkWarps - 1) / kChunkWarps;
+  const long grid = std::min<long>(need, (long)sms[dev] * occ[dev]);
+  decode_mtp_chunk_kernel<T, L2NORM><<<(unsigned)grid, kChunkWarps * 32, smem, stream>>>(q);
+  return cudaGetLastError();
+}
+
+template <bool L2NORM>
+cudaError_t launch_chunk_any(const DecodeMtpParams& p, cudaStream_t stream) {
+  static_assert(kChunkMaxT == 4, "one instantiation per token count");
+  switch (p.T) {
+    case 2: return launch_chunk<2, L2NORM>(p, stream);
+    case 3: return launch_chunk<3, L2NORM>(p, stream);
+    case 4: return launch_chunk<4, L2NORM>(p, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
 }  // namespace
 
 cudaError_t launch_decode_mtp(const DecodeMtpParams& p, cudaStream_t stream) {
   if (p.B == 0 || p.T == 0) return cudaSuccess;
-  if (pipe_supported(p))
-    return (p.flags & kFlagQkL2Norm) ? launch_pipe<true>(p, stream) : launch_pipe<false>(p, stream);
+  if (pipe_supported(p)) {
+    const bool l2 = (p.flags & kFlagQkL2Norm) != 0;
+    // without intermediate states, 2 .. kChunkMaxT tokens: all tokens' products at once (at
+    // one token the two kernels do the same work and the token-serial one is a little faster)
+    if (!p.inter && p.T >= 2 && p.T <= kChunkMaxT)
+      return l2 ? launch_chunk_any<true>(p, stream) : launch_chunk_any<false>(p, stream);
+    return l2 ? launch_pipe<true>(p, stream) : launch_pipe<false>(p, stream);
+  }
   return decode_rows_for(p.B, p.HV) == 32 ? launch_mtp_rows<32>(p, stream) : launch_mtp_rows<16>(p, stream);
 }
 

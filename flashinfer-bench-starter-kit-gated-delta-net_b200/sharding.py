@@ -72,6 +72,47 @@ def plan_prefill(seqlens, num_v_heads: int, world: int, head_group: int = 2) -> 
             for r in range(world)]
 
 
+def prefill_shard_calls(shard: PrefillShard, seqlens, q, k, v, state, A_log, a, dt_bias, b, output, new_state,
+                        cu_dtype=None):
+    """The prefill calls of one rank's share, as keyword arguments for
+    ``kernel_prefill.run_dps``: one call per contiguous run of the shard's sequences,
+    every tensor a view of the full call's tensors restricted to the run's tokens and
+    the shard's v-head range (q/k to the q/k heads those v-heads read), so the rank
+    writes its part of ``output`` and ``new_state`` in place and nothing is copied
+    except each run's small ``cu_seqlens``.  ``seqlens`` are the host-side lengths the
+    plan was made from; ``state`` may be None (zeros)."""
+    import torch
+
+    lens = [int(x) for x in seqlens]
+    HQ, HV = q.shape[1], v.shape[1]
+    if HV % HQ:
+        raise ValueError(f"{HV} v-heads do not map onto {HQ} q/k heads")
+    ratio = HV // HQ
+    lo, hi = shard.head_lo, shard.head_hi
+    if lo % ratio or hi % ratio:
+        raise ValueError(f"v-head range [{lo}, {hi}) splits a q/k head (GVA ratio {ratio})")
+    starts = [0]
+    for n in lens:
+        starts.append(starts[-1] + n)
+    runs = []
+    for i in sorted(shard.seqs):
+        if runs and runs[-1][1] == i:
+            runs[-1][1] = i + 1
+        else:
+            runs.append([i, i + 1])
+    cu_dtype = cu_dtype or torch.int32
+    calls = []
+    for s0, s1 in runs:
+        t0, t1 = starts[s0], starts[s1]
+        cu = torch.tensor([x - t0 for x in starts[s0:s1 + 1]], dtype=cu_dtype, device=q.device)
+        calls.append(dict(
+            q=q[t0:t1, lo // ratio:hi // ratio], k=k[t0:t1, lo // ratio:hi // ratio], v=v[t0:t1, lo:hi],
+            state=None if state is None else state[s0:s1, lo:hi], A_log=A_log[lo:hi], a=a[t0:t1, lo:hi],
+            dt_bias=dt_bias[lo:hi], b=b[t0:t1, lo:hi], cu_seqlens=cu, output=output[t0:t1, lo:hi],
+            new_state=new_state[s0:s1, lo:hi]))
+    return calls
+
+
 def gather_to_rank0(tensor, group=None):
     """Optional NCCL gather of equally-shaped per-rank outputs onto rank 0
     (``all_gather`` over NVLink; never on the timed hot path).  Returns the list

@@ -163,3 +163,34 @@ def test_index_beyond_pool_sets_device_error(gdn):
     torch.cuda.synchronize()
     assert gdn._lib.device_error(clear=True) & gdn._lib.GDN_DEVERR_BAD_INDEX
     assert not out[1].float().abs().any()
+
+
+@pytest.mark.parametrize("T,l2", [(2, False), (2, True), (3, True), (4, False), (4, True)])
+def test_chunked_tokens_match_token_serial_kernel(gdn, T, l2):
+    """2 to 4 tokens without intermediate states run the chunked kernel (every token's
+    products with the state from the item's initial rows, the token recurrence on
+    scalars through the Gram matrix of q and k); a call that also asks for the
+    intermediate states runs the token-serial kernel.  Both must give the same outputs
+    and final states on the same inputs, within fp32 rounding."""
+    B, P = 37, 40  # 37 x 32 x 16 items: several per warp, padded entries among them
+    d = mtp_inputs(gdn, B=B, T=T, P=P, seed=250 + T)
+    if l2:
+        d["q"] = (d["q"].float() * 3.0).bfloat16()
+        d["k"] = (d["k"].float() * 0.5).bfloat16()
+    idx = list(np.random.default_rng(250 + T).permutation(P)[:B])
+    idx[3] = idx[20] = -1
+    c = {k: v.cuda() for k, v in d.items()}
+    ix = torch.tensor(idx, device="cuda")
+    out1, fin1 = gdn.kernel_mtp.run(c["q"], c["k"], c["v"], c["pool"], ix, c["A_log"], c["a"], c["dt_bias"],
+                                    c["b"], None, use_qk_l2norm=l2)
+    inter = torch.empty(P, T, 32, 128, 128, device="cuda")
+    out2, fin2 = gdn.kernel_mtp.run(c["q"], c["k"], c["v"], c["pool"], ix, c["A_log"], c["a"], c["dt_bias"],
+                                    c["b"], None, inter, use_qk_l2norm=l2)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(fin1, fin2, atol=2e-6, rtol=1e-5)
+    torch.testing.assert_close(out1.float(), out2.float(), atol=1e-3, rtol=2 ** -7)
+    assert torch.equal(fin1[[i for i in range(P) if i not in idx]], c["pool"][[i for i in range(P) if i not in idx]])
+    assert not out1[3].float().abs().any() and not out1[20].float().abs().any()
+    o_ref, p_ref = oracle(d, idx, use_qk_l2norm=l2)
+    check(out1, fin1, o_ref, p_ref)
+    assert gdn._lib.device_error() == 0

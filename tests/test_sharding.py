@@ -69,3 +69,30 @@ def test_gather_to_rank0_gloo_world2():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert [x for x in got if x >= 0] == list(range(10))
+
+
+def test_prefill_shard_calls_cover_every_token_and_head_once(gdn):
+    """The views a rank's share becomes (no copies but each run's cu_seqlens) tile the
+    call's (token, v-head) and (sequence, v-head) grids exactly once over the ranks,
+    for whole-sequence shards and for v-head-pair shards.  CPU tensors: views only."""
+    for lens, world in (([70, 5, 300, 64, 1], 2), ([70, 5, 300, 64, 1], 4), ([900, 257], 4), ([33], 8)):
+        T, N = sum(lens), len(lens)
+        q = torch.zeros(T, 16, 128, dtype=torch.bfloat16)
+        v = torch.zeros(T, 32, 128, dtype=torch.bfloat16)
+        ab = torch.zeros(T, 32, dtype=torch.bfloat16)
+        par = torch.zeros(32)
+        out = torch.zeros(T, 32, 128, dtype=torch.bfloat16)
+        ns = torch.zeros(N, 32, 4, 4)
+        seen_tok = torch.zeros(T, 32, dtype=torch.int32)
+        seen_seq = torch.zeros(N, 32, dtype=torch.int32)
+        for shard in gdn.sharding.plan_prefill(lens, 32, world):
+            for c in gdn.sharding.prefill_shard_calls(shard, lens, q, q, v, None, par, ab, par, ab, out, ns):
+                t0 = (c["output"].data_ptr() - out.data_ptr()) // (out.stride(0) * 2)
+                h0 = (c["v"].data_ptr() - v.data_ptr()) // 2 % (32 * 128) // 128
+                nt, nh = c["output"].shape[0], c["output"].shape[1]
+                assert c["q"].shape[1] * 2 == nh and c["a"].shape == (nt, nh) and c["A_log"].shape == (nh,)
+                assert int(c["cu_seqlens"][-1]) == nt and c["cu_seqlens"].dtype == torch.int32
+                seen_tok[t0:t0 + nt, h0:h0 + nh] += 1
+                s0 = (c["new_state"].data_ptr() - ns.data_ptr()) // (ns.stride(0) * 4)
+                seen_seq[s0:s0 + c["new_state"].shape[0], h0:h0 + nh] += 1
+        assert bool((seen_tok == 1).all()) and bool((seen_seq == 1).all()), (lens, world)
