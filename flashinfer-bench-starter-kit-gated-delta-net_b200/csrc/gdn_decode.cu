@@ -17,6 +17,8 @@
 //     using o = scale * (g*S.q + delta * k.q), which equals scale * (S'.q).
 //   * The updated row is written straight from registers with 16 B streaming
 //     stores; o is written as bf16 by the lanes that own each row.
+//   * Pooled form (DecodeParams::indices): the same pass on slot indices[b] of a
+//     state pool, the one-token case of gdn_decode_pooled.
 #include "gdn_common.cuh"
 #include "gdn_kernels.h"
 
@@ -53,7 +55,19 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeParams p) {
     return;
   }
 
-  const size_t in_off = (size_t)bi * p.s_sb + (size_t)h * p.s_sh + (size_t)row0 * kHeadDim;
+  // the state block of sequence bi: its own, or slot indices[bi] of a pool
+  int64_t slot = bi;
+  if (p.indices) {
+    slot = p.idx_is_int64 ? reinterpret_cast<const int64_t*>(p.indices)[bi]
+                          : (int64_t) reinterpret_cast<const int32_t*>(p.indices)[bi];
+    if (slot < 0 || slot >= p.P) {  // padded (or out-of-range) entry: zero outputs, no state touched
+      if (slot >= p.P && threadIdx.x == 0) raise_device_error(kDevErrBadIndex);
+      if (threadIdx.x < ROWS)
+        p.out[(size_t)bi * p.o_sb + (size_t)h * p.o_sh + row0 + threadIdx.x] = __float2bfloat16_rn(0.f);
+      return;
+    }
+  }
+  const size_t in_off = (size_t)slot * p.s_sb + (size_t)h * p.s_sh + (size_t)row0 * kHeadDim;
   if (threadIdx.x == 0 && has_state) {
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) mbar_init(&bars[w], 1);
@@ -92,7 +106,7 @@ __global__ void __launch_bounds__(128) decode_kernel(DecodeParams p) {
   const float* wtile = tile + warp * kRowsPerWarp * kHeadDim;
   if (has_state && !mbar_wait(&bars[warp], 0)) return;
 
-  float* dst = p.new_state + (size_t)bi * p.n_sb + (size_t)h * p.n_sh + (size_t)wrow0 * kHeadDim + lane * 4;
+  float* dst = p.new_state + (size_t)slot * p.n_sb + (size_t)h * p.n_sh + (size_t)wrow0 * kHeadDim + lane * 4;
   float o_mine = 0.0f;
 #pragma unroll 4
   for (int r = 0; r < kRowsPerWarp; ++r) {

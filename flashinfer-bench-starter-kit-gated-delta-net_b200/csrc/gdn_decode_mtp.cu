@@ -1053,10 +1053,47 @@ cudaError_t launch_chunk_any(const DecodeMtpParams& p, cudaStream_t stream) {
 
 cudaError_t launch_decode_mtp(const DecodeMtpParams& p, cudaStream_t stream) {
   if (p.B == 0 || p.T == 0) return cudaSuccess;
+  if (p.T == 1 && !p.inter) {
+    // one token, no intermediate states: the single-token decode kernel on the indexed slots
+    DecodeParams d;
+    d.q = p.q;
+    d.k = p.k;
+    d.v = p.v;
+    d.state = p.pool;
+    d.A_log = p.A_log;
+    d.a = p.a;
+    d.dt_bias = p.dt_bias;
+    d.b = p.b;
+    d.out = p.out;
+    d.new_state = p.new_pool;
+    d.q_sb = p.q_sb;
+    d.q_sh = p.q_sh;
+    d.k_sb = p.k_sb;
+    d.k_sh = p.k_sh;
+    d.v_sb = p.v_sb;
+    d.v_sh = p.v_sh;
+    d.s_sb = p.s_sn;
+    d.s_sh = p.s_sh;
+    d.a_sb = p.a_sb;
+    d.b_sb = p.b_sb;
+    d.o_sb = p.o_sb;
+    d.o_sh = p.o_sh;
+    d.n_sb = p.n_sn;
+    d.n_sh = p.n_sh;
+    d.scale = p.scale;
+    d.B = p.B;
+    d.HQ = p.HQ;
+    d.HV = p.HV;
+    d.ratio = p.ratio;
+    d.flags = p.flags;
+    d.indices = p.indices;
+    d.idx_is_int64 = p.idx_is_int64;
+    d.P = p.P;
+    return launch_decode(d, decode_rows_for(p.B, p.HV), stream);
+  }
   if (pipe_supported(p)) {
     const bool l2 = (p.flags & kFlagQkL2Norm) != 0;
-    // without intermediate states, 2 .. kChunkMaxT tokens: all tokens' products at once (at
-    // one token the two kernels do the same work and the token-serial one is a little faster)
+    // without intermediate states, 2 .. kChunkMaxT tokens: all tokens' products at once
     if (!p.inter && p.T >= 2 && p.T <= kChunkMaxT)
       return l2 ? launch_chunk_any<true>(p, stream) : launch_chunk_any<false>(p, stream);
     return l2 ? launch_pipe<true>(p, stream) : launch_pipe<false>(p, stream);

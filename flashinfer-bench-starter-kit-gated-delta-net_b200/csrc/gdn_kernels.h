@@ -33,6 +33,12 @@ struct DecodeParams {
   float scale;
   int B, HQ, HV, ratio;
   uint32_t flags;
+  // pooled form (one token against a state pool): sequence b reads slot indices[b] of `state`
+  // (a pool of P slots, s_sb = slot stride) and writes the same slot of `new_state`; a negative
+  // index is a padded entry (zero outputs), one >= P raises GDN_DEVERR_BAD_INDEX
+  const void* indices = nullptr;
+  int idx_is_int64 = 0;
+  int64_t P = 0;
 };
 
 struct PrefillParams {

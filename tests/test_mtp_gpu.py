@@ -194,3 +194,53 @@ def test_chunked_tokens_match_token_serial_kernel(gdn, T, l2):
     o_ref, p_ref = oracle(d, idx, use_qk_l2norm=l2)
     check(out1, fin1, o_ref, p_ref)
     assert gdn._lib.device_error() == 0
+
+
+@pytest.mark.parametrize("T", [3, 4])
+def test_fused_projection_views(gdn, T):
+    """q, k, v as views of one fused projection buffer [B, T, HQ + HQ + HV + 8, 128] (every
+    batch, token and head stride differs from a contiguous tensor; rows stay 16-byte aligned):
+    same results as contiguous copies."""
+    B, P, HQ, HV = 6, 9, 16, 32
+    d = mtp_inputs(gdn, B=B, T=T, P=P, seed=260 + T)
+    idx = [4, -1, 0, 8, 2, 6]
+    c = {k: v.cuda() for k, v in d.items()}
+    buf = torch.zeros(B, T, 2 * HQ + HV + 8, 128, dtype=torch.bfloat16, device="cuda")
+    buf[:, :, :HQ] = c["q"]
+    buf[:, :, HQ:2 * HQ] = c["k"]
+    buf[:, :, 2 * HQ:2 * HQ + HV] = c["v"]
+    q, k, v = buf[:, :, :HQ], buf[:, :, HQ:2 * HQ], buf[:, :, 2 * HQ:2 * HQ + HV]
+    assert not q.is_contiguous() and q.stride(1) == (2 * HQ + HV + 8) * 128
+    ix = torch.tensor(idx, device="cuda")
+    o1, f1 = gdn.kernel_mtp.run(q, k, v, c["pool"], ix, c["A_log"], c["a"], c["dt_bias"], c["b"], None)
+    o2, f2 = gdn.kernel_mtp.run(c["q"], c["k"], c["v"], c["pool"], ix, c["A_log"], c["a"], c["dt_bias"], c["b"],
+                                None)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(f1, f2)
+    o_ref, p_ref = oracle(d, idx)
+    check(o1, f1, o_ref, p_ref)
+
+
+def test_one_token_in_place_padding_and_bad_index(gdn):
+    """One token without intermediate states runs the single-token decode kernel on the
+    indexed slots: in place (the pool is its own output), a padded entry leaves zeros and
+    touches no slot, an index beyond the pool raises GDN_DEVERR_BAD_INDEX."""
+    B, P = 5, 7
+    d = mtp_inputs(gdn, B=B, T=1, P=P, seed=270)
+    idx = [6, -1, 0, 3, 1]
+    c = {k: v.cuda() for k, v in d.items()}
+    pool = c["pool"].clone()
+    out = torch.empty(B, 1, 32, 128, dtype=torch.bfloat16, device="cuda")
+    gdn._lib.device_error(clear=True)
+    gdn.kernel_mtp.run_dps(c["q"], c["k"], c["v"], pool, torch.tensor(idx, device="cuda", dtype=torch.int32),
+                           c["A_log"], c["a"], c["dt_bias"], c["b"], None, out, pool)
+    torch.cuda.synchronize()
+    o_ref, p_ref = oracle(d, idx)
+    check(out, pool, o_ref, p_ref)
+    assert not out[1].float().abs().any()
+    assert torch.equal(pool[[2, 4, 5]], c["pool"][[2, 4, 5]])  # slots no entry names
+    assert gdn._lib.device_error(clear=True) == 0
+    out2, _ = run_gpu(gdn, d, [0, 9, 2, 3, 4])
+    torch.cuda.synchronize()
+    assert gdn._lib.device_error(clear=True) & gdn._lib.GDN_DEVERR_BAD_INDEX
+    assert not out2[1].float().abs().any()
