@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(kPipeWarps * 32, 4) decode_mtp_pipe_kernel(Dec
 // ---------------------------------------------------------------------------
 // Chunked multi-token kernel (2 <= T <= kChunkMaxT tokens, no intermediate states,
 // q/k/v rows 16-byte aligned): every token's dot products with the state come
-// from the item's initial rows at once instead of one token after another.
+// from the unit's initial rows at once instead of one token after another.
 //
 // For one state row s and tokens t = 0 .. T-1 the decode recurrence is
 //   s_t = g_t s_{t-1} + d_t k_t,   d_t = beta_t (v_t - g_t s_{t-1}.k_t),
@@ -560,21 +560,26 @@ __global__ void __launch_bounds__(kPipeWarps * 32, 4) decode_mtp_pipe_kernel(Dec
 // products with the initial row and the Gram scalars of the token vectors:
 //   z_t(w) = s_t.w = g_t z_{t-1}(w) + d_t (k_t.w),   z_{-1}(w) = s.w,
 // and the final row is s_{T-1} = (prod_t g_t) s + sum_j c_j k_j with
-// c_j = d_j prod_{i>j} g_i.  Per unit of 16 rows of one (sequence, v-head), the
-// token rows, gates and (G) once, then (A)-(C) for each 8-row half:
-//   A  the 2T products s.k_t, s.q_t of each row, all independent, reduced
-//      together over the row's 8 lanes (the only products with the state);
+// c_j = d_j prod_{i>j} g_i.  Per work unit of 16 rows of one (sequence, v-head):
 //   G  the T^2 Gram scalars k_j.k_t (j < t) and k_j.q_t (j <= t) (+ |k_t|^2 and
 //      |q_t|^2 for the in-kernel L2 norm), each lane over 4 of the 128
 //      features, reduce-scattered over the warp into shared memory;
-//   B  the recurrence on scalars per row (z, d_t, o_t, c_j);
-//   C  one pass over the row: s <- (prod g) s + sum_j c_j k_j.
-// Against the token-serial form this takes one reduction round per row pair
-// instead of one per token and one multiply-add per token and element in the
-// state update, and no token waits for the previous one.  The state still
-// crosses HBM once per call; each unit's rows and token rows are bulk-copied
-// one unit ahead (one stage each: the tokens are widened to fp32 at the start of
-// the unit and the rows move to registers half by half, which frees the buffers).
+//   A  S [16 x 128] times W [128 x 8] (the token vectors k_0.., q_0.., zero
+//      padded to 8) on the warp's tensor cores (mma.sync m16n8k8, tf32 inputs,
+//      fp32 accumulation; S split as tf32 hi + lo, so the products keep ~20
+//      bits; k and q are bf16 values, exact in tf32);
+//   B  the recurrence on scalars for the lane's two rows (z, d_t, o_t, c_j);
+//   C  S <- (prod g) S + C K, the rank-T update as a second mma with the state
+//      as the accumulator (c split as tf32 hi + lo), stored from the fragments.
+// The k dimension of A is permuted within each 8-column step (logical columns
+// t and t + 4 are physical columns 2t and 2t + 1), which makes the A fragment of
+// step n the accumulator fragment of columns 8n .. 8n + 7: each lane holds its 64
+// state values once, in that layout, for both products.  Against the
+// token-serial form there is no shuffle reduction per token, one multiply-add per
+// token and element in the state update, and no token waits for the previous
+// one.  The state crosses HBM once per call; each unit's rows (into padded
+// shared rows, so the fragment loads are free of bank conflicts) and token rows
+// are bulk-copied one unit ahead.
 constexpr int kChunkMaxT = 4;
 constexpr int kChunkWarps = 4;
 
@@ -639,6 +644,7 @@ constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n / 2); }
 // prepared once per unit and serve both halves.
 constexpr int kChunkRows = 16;
 constexpr uint32_t kChunkRowBytes = kChunkRows * kHeadDim * 4;  // 8192
+constexpr int kPadRow = kHeadDim + 8;                           // padded shared row (floats): 544 B
 // token rows of a unit: q and k (256 B each) per token, then v of the unit's 16 rows (32 B) per token
 __host__ __device__ constexpr uint32_t chunk_tok_bytes(int T) { return (uint32_t)T * (2 * kHeadDim * 2 + kChunkRows * 2); }
 // per token in shared memory: v of the 16 rows, g, beta (fp32)
@@ -646,10 +652,10 @@ constexpr int kChunkScal = kChunkRows + 2;
 
 template <int T, bool L2NORM>
 __host__ __device__ constexpr uint32_t chunk_warp_bytes() {
-  // rows [16][128] fp32 | token rows | q, k widened [2T][128] fp32 | Gram scalars | per-token scalars |
-  // 2 mbarriers
-  return kChunkRowBytes + chunk_tok_bytes(T) + 2u * T * kHeadDim * 4 + ChunkGram<T, L2NORM>::kBytes +
-         (uint32_t)((T * kChunkScal * 4 + 15) / 16 * 16) + 16;
+  // rows [16][kPadRow] fp32 | token rows | q, k widened [8][kPadRow] fp32 (rows >= 2T zero) |
+  // Gram scalars | per-token scalars | 2 mbarriers
+  return (uint32_t)(kChunkRows * kPadRow * 4) + chunk_tok_bytes(T) + (uint32_t)(8 * kPadRow * 4) +
+         ChunkGram<T, L2NORM>::kBytes + (uint32_t)((T * kChunkScal * 4 + 15) / 16 * 16) + 16;
 }
 
 // unit u = (b * HV + h) * 8 + row block of 16 (the division by HV as in pipe_item)
@@ -663,6 +669,24 @@ __device__ __forceinline__ PipeItem chunk_unit(int u, const DecodeMtpParams& p) 
 }
 static_assert(kHeadDim / kChunkRows == 8, "8 row blocks per head");
 
+// x = hi + lo: hi = x with the 13 mantissa bits below tf32 cleared (exactly a tf32 value), lo =
+// x - hi (exact in fp32); the tensor core reads lo as tf32, dropping its low 13 bits, so the pair
+// keeps about 20 significant bits of x (two integer/float instructions, no rounding mode emulation)
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  hi = __float_as_uint(x) & 0xffffe000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
+}
+// d += a b, m16n8k8, tf32 inputs, fp32 accumulation (fragments as in the PTX ISA:
+// lane = 4 g + t; a: (g, t), (g + 8, t), (g, t + 4), (g + 8, t + 4); b: (t, g), (t + 4, g);
+// d: (g, 2t), (g, 2t + 1), (g + 8, 2t), (g + 8, 2t + 1))
+__device__ __forceinline__ void mma_16x8x8_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 template <int T, bool L2NORM>
 __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(DecodeMtpParams p) {
   using G = ChunkGram<T, L2NORM>;
@@ -670,10 +694,10 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* wbase = smem_raw + (size_t)warp * chunk_warp_bytes<T, L2NORM>();
-  float* rows_buf = reinterpret_cast<float*>(wbase);
-  unsigned char* tok_buf = wbase + kChunkRowBytes;
-  float* qk32 = reinterpret_cast<float*>(tok_buf + kTok);  // [2T][128]: k_0 .. k_{T-1}, q_0 .. q_{T-1}
-  float* gram = qk32 + 2 * T * kHeadDim;
+  float* rows_buf = reinterpret_cast<float*>(wbase);  // [16][kPadRow]
+  unsigned char* tok_buf = wbase + kChunkRows * kPadRow * 4;
+  float* qk32 = reinterpret_cast<float*>(tok_buf + kTok);  // [8][kPadRow]: k_0 .. k_{T-1}, q_0 .. q_{T-1}, 0 ..
+  float* gram = qk32 + 8 * kPadRow;
   float* scal = gram + G::kBytes / 4;  // [T][kChunkScal]: v of rows 0-15, g, beta
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       reinterpret_cast<unsigned char*>(scal) + (T * kChunkScal * 4 + 15) / 16 * 16);  // rows, tokens
@@ -681,26 +705,28 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
   const int n_units = p.B * p.HV * (kHeadDim / kChunkRows);  // < 2^31 (checked by the launcher)
   const int first = blockIdx.x * kChunkWarps + warp, step = gridDim.x * kChunkWarps;
   if (first >= n_units) return;
-  const int rg = lane >> 3, cs = lane & 7;
+  const int g8 = lane >> 2, t4 = lane & 3;  // mma fragment coordinates
 
   if (lane == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     fence_barrier_init();
   }
+  // the zero padding vectors (w >= 2T) of W, written once
+  for (int e = lane; e < (8 - 2 * T) * kPadRow; e += 32) qk32[2 * T * kPadRow + e] = 0.f;
   __syncwarp();
 
   auto issue_rows = [&](const PipeItem& it, int64_t slot) {
+    const bool have = slot >= 0 && slot < p.P;
     if (lane == 0) {
-      if (slot >= 0 && slot < p.P) {
-        mbar_arrive_expect_tx(&bars[0], kChunkRowBytes);
-        bulk_g2s_evict_first(rows_buf,
-                             p.pool + (size_t)slot * p.s_sn + (size_t)it.h * p.s_sh + (size_t)it.wrow0 * kHeadDim,
-                             kChunkRowBytes, &bars[0]);
-      } else {
-        mbar_arrive(&bars[0]);  // nothing to load: complete the phase
-      }
+      if (have) mbar_arrive_expect_tx(&bars[0], kChunkRowBytes);
+      else mbar_arrive(&bars[0]);  // nothing to load: complete the phase
     }
+    __syncwarp();
+    if (have && lane < kChunkRows)  // one 512-byte row per lane, into its padded shared row
+      bulk_g2s_evict_first(rows_buf + lane * kPadRow,
+                           p.pool + (size_t)slot * p.s_sn + (size_t)it.h * p.s_sh + (size_t)(it.wrow0 + lane) * kHeadDim,
+                           kHeadDim * 4, &bars[0]);
   };
   auto issue_tok = [&](const PipeItem& it) {
     if (lane == 0) mbar_arrive_expect_tx(&bars[1], kTok);
@@ -765,7 +791,7 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
       const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
       const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
       wv[w] = make_float4(lo.x, lo.y, hi.x, hi.y);
-      *reinterpret_cast<float4*>(qk32 + w * kHeadDim + lane * 4) = wv[w];
+      *reinterpret_cast<float4*>(qk32 + w * kPadRow + lane * 4) = wv[w];
     }
     {
       const __nv_bfloat16* vt = reinterpret_cast<const __nv_bfloat16*>(tok_buf + T * 512);
@@ -802,71 +828,73 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
         if ((lane & ((1 << sh) - 1)) == 0) gram[lane >> sh] = gp[0];
       }
     }
+
+    // ---- the unit's 16 rows -> registers in the mma accumulator layout: c[n] = rows g8 and
+    //      g8 + 8, columns 8 n + 2 t4 and 8 n + 2 t4 + 1; then the rows buffer goes to the next unit ----
     if (!mbar_wait(&bars[0], rows_done & 1)) { fail = true; break; }
     ++rows_done;
-    __syncwarp();  // Gram scalars written
-    float nkv[T], nqv[T];  // 1 / |k_t|, 1 / |q_t| with the L2 norm, else 1
+    float c[16][4];
+    if (valid) {
 #pragma unroll
-    for (int t = 0; t < T; ++t) {
-      nkv[t] = L2NORM ? rsqrtf(gram[G::nk(t)] + 1e-6f) : 1.f;
-      nqv[t] = L2NORM ? rsqrtf(gram[G::nq(t)] + 1e-6f) : 1.f;
+      for (int n = 0; n < 16; ++n) {
+        const float2 x0 = *reinterpret_cast<const float2*>(rows_buf + g8 * kPadRow + 8 * n + 2 * t4);
+        const float2 x1 = *reinterpret_cast<const float2*>(rows_buf + (g8 + 8) * kPadRow + 8 * n + 2 * t4);
+        c[n][0] = x0.x;
+        c[n][1] = x0.y;
+        c[n][2] = x1.x;
+        c[n][3] = x1.y;
+      }
     }
-
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
-      // ---- this half's 8 rows -> registers (after the second half the rows buffer is free) ----
-      float2 s[2][8];
-      if (valid) {
+    __syncwarp();  // rows read; Gram scalars written
+    if (more) {
+      issue_rows(nx, slot_next);
+      ++rows_issued;
+    }
+    __nv_bfloat16* out_unit = p.out + (size_t)it.bi * p.o_sb + (size_t)it.h * p.o_sh + it.wrow0;
+    if (!valid) {
+      if (slot >= p.P && lane == 0) raise_device_error(kDevErrBadIndex);
+      for (int e = lane; e < T * kChunkRows; e += 32)
+        out_unit[(size_t)(e >> 4) * p.o_st + (e & 15)] = __float2bfloat16_rn(0.f);
+    } else {
+      // ---- A: D = S W (rows g8, g8 + 8 of the unit; token vectors 2 t4, 2 t4 + 1) ----
+      // four independent accumulators (hi / lo x even / odd steps) keep the mma chains short
+      float da[4][4] = {};
 #pragma unroll
-        for (int ps = 0; ps < 2; ++ps) {
-          const float* src = rows_buf + (half * 8 + ps * 4 + rg) * kHeadDim + cs * 4;
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            const float4 x = *reinterpret_cast<const float4*>(src + c4 * 32);
-            s[ps][2 * c4] = make_float2(x.x, x.y);
-            s[ps][2 * c4 + 1] = make_float2(x.z, x.w);
-          }
-        }
+      for (int n = 0; n < 16; ++n) {
+        uint32_t ah[4], al[4];
+        tf32_split(c[n][0], ah[0], al[0]);  // (g8, logical t4)
+        tf32_split(c[n][2], ah[1], al[1]);  // (g8 + 8, t4)
+        tf32_split(c[n][1], ah[2], al[2]);  // (g8, t4 + 4)
+        tf32_split(c[n][3], ah[3], al[3]);  // (g8 + 8, t4 + 4)
+        const float2 bw = *reinterpret_cast<const float2*>(qk32 + g8 * kPadRow + 8 * n + 2 * t4);  // vector g8
+        const uint32_t b0 = __float_as_uint(bw.x), b1 = __float_as_uint(bw.y);
+        mma_16x8x8_tf32(da[2 * (n & 1)], ah[0], ah[1], ah[2], ah[3], b0, b1);
+        mma_16x8x8_tf32(da[2 * (n & 1) + 1], al[0], al[1], al[2], al[3], b0, b1);
       }
-      if (half == 1) {
-        __syncwarp();
-        if (more) {
-          issue_rows(nx, slot_next);
-          ++rows_issued;
-        }
-      }
-      const int r0 = it.wrow0 + half * 8;
-      __nv_bfloat16* out_half = p.out + (size_t)it.bi * p.o_sb + (size_t)it.h * p.o_sh + r0;
-      if (!valid) {
-        if (half == 0 && slot >= p.P && lane == 0) raise_device_error(kDevErrBadIndex);
-        for (int e = lane; e < T * 8; e += 32)
-          out_half[(size_t)(e >> 3) * p.o_st + (e & 7)] = __float2bfloat16_rn(0.f);
-        continue;
-      }
-      // ---- A: s.k_t and s.q_t of both rows, each reduced over the row's 8 lanes ----
-      float x[2][2 * T];
+      float dacc[4];
 #pragma unroll
-      for (int w = 0; w < 2 * T; ++w) {
-        float2 a0 = make_float2(0.f, 0.f), a1 = a0;
+      for (int i = 0; i < 4; ++i) dacc[i] = (da[0][i] + da[2][i]) + (da[1][i] + da[3][i]);
+      // every lane of the quad gathers all 2T products of rows g8 and g8 + 8
+      float x[2][8];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          const float4 f = *reinterpret_cast<const float4*>(qk32 + w * kHeadDim + c4 * 32 + cs * 4);
-          const float2 lo = make_float2(f.x, f.y), hi = make_float2(f.z, f.w);
-          a0 = __ffma2_rn(s[0][2 * c4], lo, a0);
-          a1 = __ffma2_rn(s[1][2 * c4], lo, a1);
-          a0 = __ffma2_rn(s[0][2 * c4 + 1], hi, a0);
-          a1 = __ffma2_rn(s[1][2 * c4 + 1], hi, a1);
-        }
-        float2 r = __fadd2_rn(make_float2(a0.x, a1.x), make_float2(a0.y, a1.y));
-#pragma unroll
-        for (int m = 1; m < 8; m <<= 1)
-          r = __fadd2_rn(r, make_float2(__shfl_xor_sync(0xffffffffu, r.x, m), __shfl_xor_sync(0xffffffffu, r.y, m)));
-        x[0][w] = r.x;
-        x[1][w] = r.y;
+      for (int tq = 0; tq < 4; ++tq) {
+        const int src = (lane & ~3) | tq;
+        x[0][2 * tq] = __shfl_sync(0xffffffffu, dacc[0], src);
+        x[0][2 * tq + 1] = __shfl_sync(0xffffffffu, dacc[1], src);
+        x[1][2 * tq] = __shfl_sync(0xffffffffu, dacc[2], src);
+        x[1][2 * tq + 1] = __shfl_sync(0xffffffffu, dacc[3], src);
       }
-      // ---- B: the token recurrence on scalars ----
+      // ---- B: the token recurrence on scalars for rows g8 (ps 0) and g8 + 8 (ps 1) ----
+      float nkv[T], nqv[T];  // 1 / |k_t|, 1 / |q_t| with the L2 norm, else 1
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        nkv[t] = L2NORM ? rsqrtf(gram[G::nk(t)] + 1e-6f) : 1.f;
+        nqv[t] = L2NORM ? rsqrtf(gram[G::nq(t)] + 1e-6f) : 1.f;
+      }
       const float scale = p.scale;
-      float om[2], cc[2][T];  // om: the output of token cs (this lane's store)
+      float cm[2], pg = 1.f;  // cm: c of token t4 for the lane's two rows; pg = prod g
+#pragma unroll
+      for (int t = 0; t < T; ++t) pg *= scal[t * kChunkScal + kChunkRows];
 #pragma unroll
       for (int ps = 0; ps < 2; ++ps) {
         float z[2 * T];
@@ -875,15 +903,14 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
           z[t] = x[ps][t] * nkv[t];
           z[T + t] = x[ps][T + t] * nqv[t];
         }
-        float dl[T];
-        om[ps] = 0.f;
-        const int vr = half * 8 + ps * 4 + rg;
+        const int vr = g8 + 8 * ps;
+        float dl[T], om = 0.f;  // om: the output of token t4 (this lane's store)
 #pragma unroll
         for (int t = 0; t < T; ++t) {
           const float g = scal[t * kChunkScal + kChunkRows];
           const float d = scal[t * kChunkScal + kChunkRows + 1] * (scal[t * kChunkScal + vr] - g * z[t]);
           const float o = scale * fmaf(d, gram[G::kq(t, t)] * (nkv[t] * nqv[t]), g * z[T + t]);
-          om[ps] = cs == t ? o : om[ps];
+          om = t4 == t ? o : om;
           dl[t] = d;
 #pragma unroll
           for (int t2 = t + 1; t2 < T; ++t2) {
@@ -892,53 +919,31 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
           }
         }
         float tail = 1.f;  // prod_{i > j} g_i
+        cm[ps] = 0.f;
 #pragma unroll
         for (int t = T - 1; t >= 0; --t) {
-          cc[ps][t] = dl[t] * tail * nkv[t];
+          const float cj = dl[t] * tail * nkv[t];
+          cm[ps] = t4 == t ? cj : cm[ps];
           tail *= scal[t * kChunkScal + kChunkRows];
         }
+        if (t4 < T) out_unit[(size_t)t4 * p.o_st + vr] = __float2bfloat16_rn(om);  // token t4's output
       }
-      // token cs's outputs of the lane's two rows (lanes cs < T)
-      if (cs < T) {
-        __nv_bfloat16* ot = out_half + (size_t)cs * p.o_st;
-        ot[rg] = __float2bfloat16_rn(om[0]);
-        ot[4 + rg] = __float2bfloat16_rn(om[1]);
-      }
-      // ---- C: s <- (prod g) s + sum_j c_j k_j, then the final rows ----
-      float pg = 1.f;
+      // ---- C: S <- (prod g) S + C K: A = c (rows g8, g8 + 8; token t4 < T, else 0), B = k_t4 ----
+      uint32_t ch0, cl0, ch1, cl1;
+      tf32_split(cm[0], ch0, cl0);
+      tf32_split(cm[1], ch1, cl1);
+      const float* krow = qk32 + (t4 < T ? t4 : 2 * T) * kPadRow;  // k_t4, or a zero row
+      float* dst0 = p.new_pool + (size_t)slot * p.n_sn + (size_t)it.h * p.n_sh + (size_t)(it.wrow0 + g8) * kHeadDim +
+                    2 * t4;
+      float* dst1 = dst0 + 8 * kHeadDim;
 #pragma unroll
-      for (int t = 0; t < T; ++t) pg *= scal[t * kChunkScal + kChunkRows];
-      const float2 pg2 = make_float2(pg, pg);
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float2 klo[T], khi[T];
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          const float4 f = *reinterpret_cast<const float4*>(qk32 + t * kHeadDim + c4 * 32 + cs * 4);
-          klo[t] = make_float2(f.x, f.y);
-          khi[t] = make_float2(f.z, f.w);
-        }
-#pragma unroll
-        for (int ps = 0; ps < 2; ++ps) {
-          float2 lo = __fmul2_rn(s[ps][2 * c4], pg2), hi = __fmul2_rn(s[ps][2 * c4 + 1], pg2);
-#pragma unroll
-          for (int t = 0; t < T; ++t) {
-            const float2 c2 = make_float2(cc[ps][t], cc[ps][t]);
-            lo = __ffma2_rn(c2, klo[t], lo);
-            hi = __ffma2_rn(c2, khi[t], hi);
-          }
-          s[ps][2 * c4] = lo;
-          s[ps][2 * c4 + 1] = hi;
-        }
-      }
-#pragma unroll
-      for (int ps = 0; ps < 2; ++ps) {
-        float* dst = p.new_pool + (size_t)slot * p.n_sn + (size_t)it.h * p.n_sh +
-                     (size_t)(r0 + ps * 4 + rg) * kHeadDim + cs * 4;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-          st_cs_f4(dst + c4 * 32, make_float4(s[ps][2 * c4].x, s[ps][2 * c4].y, s[ps][2 * c4 + 1].x,
-                                              s[ps][2 * c4 + 1].y));
+      for (int n = 0; n < 16; ++n) {
+        float acc[4] = {pg * c[n][0], pg * c[n][1], pg * c[n][2], pg * c[n][3]};
+        const uint32_t b0 = __float_as_uint(krow[8 * n + g8]);
+        mma_16x8x8_tf32(acc, ch0, ch1, 0u, 0u, b0, 0u);
+        mma_16x8x8_tf32(acc, cl0, cl1, 0u, 0u, b0, 0u);
+        __stcs(reinterpret_cast<float2*>(dst0 + 8 * n), make_float2(acc[0], acc[1]));
+        __stcs(reinterpret_cast<float2*>(dst1 + 8 * n), make_float2(acc[2], acc[3]));
       }
     }
     __syncwarp();  // qk32, the Gram and per-token scalars are read before the next unit overwrites them
