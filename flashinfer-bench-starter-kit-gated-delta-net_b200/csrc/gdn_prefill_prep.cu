@@ -110,19 +110,16 @@ __device__ __forceinline__ void solve_diag16(float* AT, int p, int bar) {
 }
 
 // ---- block merges on the warp-level tensor-core path (mma.sync, tf32 inputs,
-// fp32 accumulation).  Each fp32 operand x is split as hi = tf32(x), lo =
-// tf32(x - hi) and a product accumulated as lo*hi + hi*lo + hi*hi, which keeps
-// about 21 significant bits (fp32-level for these O(1) entries).  Fragments
+// fp32 accumulation).  Each fp32 operand x is split as hi + lo (split_tf32) and a
+// product accumulated as lo*hi + hi*lo + hi*hi, which keeps about 20 significant
+// bits (fp32-level for these O(1) entries; T is stored as bf16 hi + lo, ~16 bits).  Fragments
 // are read per lane from the fp32 array (m16n8k8 layouts: g = lane / 4,
 // t = lane % 4), so no operand is broadcast through shared memory.
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
+// hi = x with the 13 mantissa bits below tf32 cleared (exactly a tf32 value), lo = x - hi (exact in
+// fp32; the tensor core reads it as tf32, dropping its low 13 bits)
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = to_tf32(x);
-  lo = to_tf32(x - __uint_as_float(hi));
+  hi = __float_as_uint(x) & 0xffffe000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
 }
 __device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
