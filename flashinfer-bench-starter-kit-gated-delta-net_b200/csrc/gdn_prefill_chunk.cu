@@ -92,7 +92,7 @@ constexpr uint32_t kRowsK = 16384;
 constexpr uint32_t kSmV = 98304;       // V, plain row-major [64][128] bf16 (16 KB)
 constexpr uint32_t kSmD = 114688;      // D^T bf16 SW128 tile [128 x 64] (A of the output MMA)
 constexpr uint32_t kSmT = 131072;      // 2 stages x (T hi | T lo: 2 tiles [64 x 64]) (record bytes 0-16383)
-constexpr uint32_t kTStage = kRecT;
+constexpr uint32_t kTStage = 2 * kTTileBytes;  // full T hi | T lo tiles (no swizzle, upper blocks zero)
 constexpr uint32_t kSmP = 163840;      // P tile [64 x 64]
 constexpr uint32_t kSmO = 172032;      // output rows of one chunk, [64 tokens][128] bf16 (TMA-store source)
 constexpr uint32_t kSmGate = 188416;   // 2 stages x gate arrays (record bytes 16384-18175)
@@ -282,6 +282,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // the T buffers' core matrices above the diagonal are never copied: zero them once
+  for (int e = tid; e < (int)(2 * kTStage / 16); e += kThreads)
+    reinterpret_cast<uint4*>(sm.base + kSmT)[e] = make_uint4(0u, 0u, 0u, 0u);
+  tc::fence_proxy_async_smem();  // visible to the tensor core (async proxy) after the barrier below
   if (tid == 0) {
     for (int i = 0; i < B_COUNT; ++i)
       mbar_init(sm.bar(i), (i == B_GFREE || i == B_GFREE + 1 || i == B_S0_READY || i == B_D_READY) ? 2 : 1);
@@ -298,12 +302,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *sm.tmem_slot();
 
   // ======================================================================= TMA producer
+  // Lane 0 waits and issues; the 16 row-block copies of a chunk's T tiles are spread over
+  // lanes 0-15 (all lanes follow lane 0's outcome, so they leave the loop together).
   if (warp == kWarpTma) {
-    if (lane == 0 && nchunks > 0) {
-      tc::prefetch_tensormap(&mapK);
-      tc::prefetch_tensormap(&mapQ);
-      tc::prefetch_tensormap(&mapV);
-      tc::prefetch_tensormap(&mapO);
+    if (nchunks > 0) {
+      if (lane == 0) {
+        tc::prefetch_tensormap(&mapK);
+        tc::prefetch_tensormap(&mapQ);
+        tc::prefetch_tensormap(&mapV);
+        tc::prefetch_tensormap(&mapO);
+      }
       int issued = 0;
       for (int i = 0; i < nchunks; ++i) {
         const int s = i & 1;
@@ -313,27 +321,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         // waits in the order their phases complete: MMA2(i-2), deltas(i-2), MMA4(i-2), R(i-1).
         // One barrier counts the record's two parts and V (its phase completes once all landed;
         // V, the last, is issued once R of chunk i - 1 has read the previous V).
-        if (i >= 2 && !wait_bar(sm, sm.bar(B_T_EMPTY + s), ph)) break;
-        mbar_arrive_expect_tx(sm.bar(B_REC_FULL + s), kRecBytes + 16384);
-        bulk_g2s(sm.base + kSmT + s * kTStage, rec, kRecT, sm.bar(B_REC_FULL + s));
-        if (i >= 2 && !wait_bar(sm, sm.bar(B_GFREE + s), ph)) break;
-        bulk_g2s(sm.base + kSmGate + s * kRecGates, rec + kRecT, kRecGates, sm.bar(B_REC_FULL + s));
-        if (i >= 2 && !wait_bar(sm, sm.bar(B_KQ_EMPTY + s), ph)) break;
-        uint64_t* full = sm.bar(B_KQ_FULL + s);
-        mbar_arrive_expect_tx(full, 6 * 8192);
-        unsigned char* kq = sm.base + kSmKQ + s * kKQStage;
-#pragma unroll
-        for (int f = 0; f < 2; ++f) {  // the two 64-feature tiles: Q, Q, K
-          tc::tma_load_3d(kq + f * kKQTile, &mapQ, 64 * f, qh, z, full);
-          tc::tma_load_3d(kq + f * kKQTile + kRowsQ2, &mapQ, 64 * f, qh, z, full);
-          tc::tma_load_3d(kq + f * kKQTile + kRowsK, &mapK, 64 * f, qh, z, full);
+        int ok = 1;
+        if (lane == 0) {
+          ok = (i < 2 || wait_bar(sm, sm.bar(B_T_EMPTY + s), ph)) ? 1 : 0;
+          if (ok) mbar_arrive_expect_tx(sm.bar(B_REC_FULL + s), kRecBytes + 16384);
         }
-        if (i >= 1 && !wait_bar(sm, sm.bar(B_V_EMPTY), (i - 1) & 1)) break;
-        tc::tma_load_3d(sm.base + kSmV, &mapV, 0, h, z, sm.bar(B_REC_FULL + s));
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        if (lane < 16) {  // T hi / lo: row block rb of a tile is the run of its rb + 1 nonzero core matrices
+          const int tile = lane >> 3, rb = lane & 7;
+          bulk_g2s(sm.base + kSmT + s * kTStage + tile * kTTileBytes + rb * 1024,
+                   rec + tile * kRecTile + tri_prefix(rb) * 128, (uint32_t)(rb + 1) * 128, sm.bar(B_REC_FULL + s));
+        }
+        if (lane == 0) {
+          ok = 0;
+          if (i < 2 || wait_bar(sm, sm.bar(B_GFREE + s), ph)) {
+            bulk_g2s(sm.base + kSmGate + s * kRecGates, rec + kRecT, kRecGates, sm.bar(B_REC_FULL + s));
+            if (i < 2 || wait_bar(sm, sm.bar(B_KQ_EMPTY + s), ph)) {
+              uint64_t* full = sm.bar(B_KQ_FULL + s);
+              mbar_arrive_expect_tx(full, 6 * 8192);
+              unsigned char* kq = sm.base + kSmKQ + s * kKQStage;
+#pragma unroll
+              for (int f = 0; f < 2; ++f) {  // the two 64-feature tiles: Q, Q, K
+                tc::tma_load_3d(kq + f * kKQTile, &mapQ, 64 * f, qh, z, full);
+                tc::tma_load_3d(kq + f * kKQTile + kRowsQ2, &mapQ, 64 * f, qh, z, full);
+                tc::tma_load_3d(kq + f * kKQTile + kRowsK, &mapK, 64 * f, qh, z, full);
+              }
+              if (i < 1 || wait_bar(sm, sm.bar(B_V_EMPTY), (i - 1) & 1)) {
+                tc::tma_load_3d(sm.base + kSmV, &mapV, 0, h, z, sm.bar(B_REC_FULL + s));
+                ok = 1;
+              }
+            }
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         issued = i + 1;
       }
       // drain: the last loads have landed before the CTA can exit (bounded)
-      if (issued > 0) {
+      if (lane == 0 && issued > 0) {
         const int i = issued - 1, s = i & 1;
         wait_bar(sm, sm.bar(B_REC_FULL + s), (i >> 1) & 1);
         wait_bar(sm, sm.bar(B_KQ_FULL + s), (i >> 1) & 1);
@@ -351,9 +375,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // descriptor bases (start address of each operand buffer); per MMA step only a
       // constant is added (tc::kmajor_step / tc::mnmajor_step)
       const uint64_t dD = tc::kmajor_desc(sm.addr(kSmD), 0, 0);
-      const uint64_t dT0 = tc::kmajor_desc(sm.addr(kSmT), 0, 0);
-      const uint64_t dT1 = tc::kmajor_desc(sm.addr(kSmT + kTStage), 0, 0);
-      constexpr uint64_t kTlo = 8192 >> 4;  // T lo follows T hi in a stage
+      // T tiles without swizzle: core matrices 128 B apart along K, row blocks 1 KB apart; one
+      // MMA step of 16 columns is two core matrices (+256 B)
+      const uint64_t dT0 = tc::sdesc_noswizzle(sm.addr(kSmT), 128u, 1024u);
+      const uint64_t dT1 = tc::sdesc_noswizzle(sm.addr(kSmT + kTStage), 128u, 1024u);
+      constexpr uint64_t kTlo = kTTileBytes >> 4;  // T lo follows T hi in a stage
+      auto tstep = [](int ks) { return (uint64_t)(ks * 16); };
       const uint64_t dP = tc::kmajor_desc(sm.addr(kSmP), 0, 0);
       const uint64_t dKQ0 = tc::kmajor_desc(sm.addr(kSmKQ), 0, 0);
       const uint64_t dKQ1 = tc::kmajor_desc(sm.addr(kSmKQ + kKQStage), 0, 0);
@@ -411,13 +438,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t dT = s ? dT1 : dT0;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16_ta(d1 + 64, tmem + kTmRhi + 8 * ks, dT + kmajor_step(0, ks), id_n64, ks > 0);
+          tc::mma_bf16_ta(d1 + 64, tmem + kTmRhi + 8 * ks, dT + tstep(ks), id_n64, ks > 0);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16_ta(d1 + 64, tmem + kTmRlo + 8 * ks, dT + kmajor_step(0, ks), id_n64, true);
+          tc::mma_bf16_ta(d1 + 64, tmem + kTmRlo + 8 * ks, dT + tstep(ks), id_n64, true);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          tc::mma_bf16_ta(d1 + 64, tmem + kTmRhi + 8 * ks, dT + kTlo + kmajor_step(0, ks), id_n64, true);
+          tc::mma_bf16_ta(d1 + 64, tmem + kTmRhi + 8 * ks, dT + kTlo + tstep(ks), id_n64, true);
         tc::mma_commit(sm.bar(B_MMA2));
         tc::mma_commit(sm.bar(B_T_EMPTY + s));
         if (more) {

@@ -13,11 +13,17 @@
 // (floor(c0/64) + ceil((c1-c0)/64) <= floor(c1/64) + 1) and every slot is
 // below total_tokens / 64 + num_seqs + 1.
 //
-// Record (kRecBytes, 16-byte aligned), written by the prep kernel and copied
-// verbatim into shared memory by the chain kernel's bulk copies:
-//   [0, 8192)      T hi: SW128 tile image [64 rows t][64 cols j] bf16, K-major
-//   [8192, 16384)  T lo: same, T - hi
-//   [16384, 18176) gates: 7 x 64 fp32 (GA_* order below)
+// Record (kRecBytes, 16-byte aligned), written by the prep kernel and bulk-copied
+// into shared memory by the chain kernel:
+//   [0, 4608)      T hi: the lower triangle of T [64 rows t][64 cols j] bf16 as the 36
+//                  nonzero 8x8 core matrices of a K-major tile without swizzle, row
+//                  block by row block, core matrices 0 .. rb of row block rb contiguous
+//                  (128 B each: 8 rows of 16 B)
+//   [4608, 9216)   T lo: same, T - hi
+//   [9216, 11008)  gates: 7 x 64 fp32 (GA_* order below)
+// In shared memory a T tile is the full [8 row blocks][8 core matrices] array (1 KB per
+// row block, LBO 128 B along K, SBO 1 KB along the rows); the chain kernel zeroes its
+// T buffers once, so the core matrices above the diagonal, never copied, stay zero.
 #pragma once
 
 #include <cuda.h>
@@ -35,10 +41,15 @@ constexpr int kC = 64;  // chunk length (tokens)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-constexpr uint32_t kRecT = 16384;      // T hi | T lo tile images
-constexpr uint32_t kRecGates = 1792;   // 7 x 64 fp32
-constexpr uint32_t kRecBytes = kRecT + kRecGates;
-static_assert(kRecBytes % 16 == 0, "record alignment");
+constexpr uint32_t kTriCM = 36;                   // nonzero core matrices of a 64 x 64 lower triangle
+constexpr uint32_t kRecTile = kTriCM * 128;       // one compacted T tile: 4608 B
+constexpr uint32_t kRecT = 2 * kRecTile;          // T hi | T lo
+constexpr uint32_t kRecGates = 1792;              // 7 x 64 fp32
+constexpr uint32_t kRecBytes = kRecT + kRecGates; // 11008
+constexpr uint32_t kTTileBytes = 8192;            // a full T tile in shared memory
+static_assert(kRecBytes % 16 == 0 && kRecTile % 16 == 0, "record alignment");
+// core matrices of the compacted tile before row block rb
+__host__ __device__ constexpr uint32_t tri_prefix(int rb) { return (uint32_t)(rb * (rb + 1) / 2); }
 
 // gate arrays (per chunk, 64 tokens each), with n_t = 1 / |k_t| and m_t = 1 / |q_t| when q
 // and k are L2-normalised in the kernels (GDN_FLAG_QK_L2NORM), n_t = m_t = 1 otherwise:

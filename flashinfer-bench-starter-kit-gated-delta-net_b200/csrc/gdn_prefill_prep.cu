@@ -7,9 +7,9 @@
 //   A[t][j] = beta_t exp(g_t - g_j) k_t.k_j   (j < t),   T = (I + A)^-1
 // T is what turns the chunk's delta-rule recurrence into one product
 // (D^T = R^T T^T in the chain kernel).  This kernel writes, per (chunk slot,
-// v-head), the record described in gdn_prefill_chunk.cuh: T as bf16 hi + lo
-// SW128 tile images (ready to be bulk-copied into the chain kernel's MMA
-// operand buffers) and the chunk's gate arrays.
+// v-head), the record described in gdn_prefill_chunk.cuh: the lower triangle of T
+// as bf16 hi + lo core matrices (bulk-copied row block by row block into the chain
+// kernel's MMA operand buffers) and the chunk's gate arrays.
 //
 // CTA = two consecutive chunk slots of one v-head, 8 warps in two groups of 4
 // (group c = slot 2 * blockIdx.x + c):
@@ -406,27 +406,30 @@ __global__ void __launch_bounds__(kThreads, 4)
       named_sync(bar128, 128);
       solve_merge16(AT, gth, bar128);
       solve_merge32(AT, gth, bar128);
-      // ---- T hi / lo tile images: 16-byte chunks in address order (coalesced) ----
-#pragma unroll 2
-      for (int j = gth; j < 512; j += 128) {
-        const int r = j >> 3, c8 = (j & 7) ^ (r & 7);
-        uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = hi;
-        if (c8 * 8 <= r) {  // chunks entirely above the diagonal stay zero
-          const float4 x0 = *reinterpret_cast<const float4*>(AT + r * kLd + c8 * 8);
-          const float4 x1 = *reinterpret_cast<const float4*>(AT + r * kLd + c8 * 8 + 4);
-          float t8[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-          if (c8 * 8 + 7 > r) {  // the diagonal chunk: zero what lies above the diagonal
+      // ---- T hi / lo, compacted lower triangle (see gdn_prefill_chunk.cuh): 16-byte core-matrix
+      //      rows in address order (coalesced) ----
+#pragma unroll 1
+      for (int q = gth; q < (int)kTriCM * 8; q += 128) {
+        const int cm = q >> 3, i = q & 7;  // core matrix (row block rb, column block kc), row i
+        int rb = 0;
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              if (c8 * 8 + e > r) t8[e] = 0.f;
-          }
-          split2(t8[0], t8[1], hi.x, lo.x);
-          split2(t8[2], t8[3], hi.y, lo.y);
-          split2(t8[4], t8[5], hi.z, lo.z);
-          split2(t8[6], t8[7], hi.w, lo.w);
+        for (int b = 1; b < 8; ++b) rb += (int)tri_prefix(b) <= cm ? 1 : 0;
+        const int kc = cm - (int)tri_prefix(rb), r = rb * 8 + i;
+        const float4 x0 = *reinterpret_cast<const float4*>(AT + r * kLd + kc * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(AT + r * kLd + kc * 8 + 4);
+        float t8[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        if (kc == rb) {  // the diagonal block: zero what lies above the diagonal
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e > i) t8[e] = 0.f;
         }
-        *reinterpret_cast<uint4*>(rec + j * 16) = hi;
-        *reinterpret_cast<uint4*>(rec + 8192 + j * 16) = lo;
+        uint4 hi, lo;
+        split2(t8[0], t8[1], hi.x, lo.x);
+        split2(t8[2], t8[3], hi.y, lo.y);
+        split2(t8[4], t8[5], hi.z, lo.z);
+        split2(t8[6], t8[7], hi.w, lo.w);
+        *reinterpret_cast<uint4*>(rec + q * 16) = hi;
+        *reinterpret_cast<uint4*>(rec + kRecTile + q * 16) = lo;
       }
     }
   }

@@ -46,6 +46,17 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr, uint32_t lbo
   return d;
 }
 
+// Shared-memory matrix descriptor for a K-major tile without swizzle: 8-row x 16-byte core
+// matrices, `lbo_bytes` apart along K and `sbo_bytes` apart along M (or N).
+__device__ __forceinline__ uint64_t sdesc_noswizzle(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  return d;                // layout type 0: no swizzle
+}
+
 // K-major operand: rows are M (or N) indices, K along the 128 B row.
 // `tile0` is the first 64-column tile; `tile_bytes` the stride between the
 // 64-column tiles; k_step = 16 columns.

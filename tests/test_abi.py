@@ -92,14 +92,14 @@ def test_prefill_rejects_bad_arguments(lib):
 
 
 def test_workspace_size(lib):
-    """One 18,176-byte record (T hi/lo tiles + 7 gate arrays) per chunk slot and
+    """One 11,008-byte record (the lower triangle of T hi and lo + 7 gate arrays) per chunk slot and
     v-head; slots = total_tokens // 64 + num_seqs + 1.  In-kernel q/k normalisation
     adds one (1/|q|, log2 1/|q|) float pair per token and v-head after the records,
     256-byte aligned.  The forced token-serial path needs no workspace."""
     a = lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
     assert a == lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0)
-    assert a == (34000 // 64 + 16 + 1) * 32 * 18176
-    assert lib.gdn_prefill_workspace_size(8, 8 * 32768, 16, 32, 128, 0) == (4096 + 9) * 32 * 18176
+    assert a == (34000 // 64 + 16 + 1) * 32 * 11008
+    assert lib.gdn_prefill_workspace_size(8, 8 * 32768, 16, 32, 128, 0) == (4096 + 9) * 32 * 11008
     # GDN_FLAG_QK_L2NORM
     assert lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0x1) == ((a + 255) & ~255) + 34000 * 32 * 8
     assert lib.gdn_prefill_workspace_size(16, 34000, 16, 32, 128, 0x2) == 0  # GDN_FLAG_PREFILL_SERIAL
@@ -112,7 +112,7 @@ def test_workspace_size_with_segments(lib):
     with 32 v-heads (32 chains on 148 SMs) gets S = 5 (pass 1: 224 CTAs in 2 waves,
     reruns: 128 in 1 wave, 3/5 of one chain's length); many or short sequences get none."""
     seg = lambda n: (n & 15) << 8  # noqa: E731  (GDN_PREFILL_SEGMENTS)
-    rec = lambda n, t: (t // 64 + n + 1) * 32 * 18176  # noqa: E731
+    rec = lambda n, t: (t // 64 + n + 1) * 32 * 11008  # noqa: E731
     st = 128 * 128 * 4
     assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(3)) == rec(2, 3000) + 2 * 32 * st * 4
     assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(2)) == rec(2, 3000) + 2 * 32 * st * 1

@@ -65,7 +65,7 @@ def test_automatic_segments_one_long_sequence(gdn):
     the library splits the sequence (its workspace grows by the segment scratch)."""
     T = 64 * 70 + 9
     inp = gdn.workloads.prefill_inputs([T], seed=310)
-    records = (T // 64 + 1 + 1) * 32 * 18176
+    records = (T // 64 + 1 + 1) * 32 * 11008
     assert gdn.kernel_prefill.workspace_size(1, T, 16, 32) > records
     assert gdn.kernel_prefill.workspace_size(1, T, 16, 32, segments=1) == records
     out, ns = gdn.kernel_prefill.run(**to_dev(inp))
@@ -138,7 +138,7 @@ def test_state_map_automatic_segments_one_long_sequence(gdn):
     inp = gdn.workloads.prefill_inputs([T], seed=335)
     inp["A_log"] = torch.full_like(inp["A_log"], -6.0)
     lib = gdn._lib.library()
-    records = (T // 64 + 2) * 32 * 18176
+    records = (T // 64 + 2) * 32 * 11008
     assert lib.gdn_prefill_workspace_size(1, T, 16, 32, 128, gdn._lib.GDN_FLAG_STATE_MAP) > records
     dev = to_dev(inp)
     M, C = gdn.kernel_prefill.state_map(dev["q"], dev["k"], dev["v"], dev["A_log"], dev["a"], dev["dt_bias"],
