@@ -773,7 +773,7 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
     const bool more = u + step < n_units;
     // this unit's gates (lane t: token t), then the next unit's inputs and the pool index after it
     float g_l = 0.f, beta_l = 0.f;
-    if (lane < T) gdn_gates(alog, ga, dtb, gb, g_l, beta_l);
+    if (lane < T) gdn_gates_fast(alog, ga, dtb, gb, g_l, beta_l);
     load_gate_inputs(nx, more, ga, gb, alog, dtb);
     const bool more2 = u + 2 * step < n_units;
     const PipeItem nn = chunk_unit(more2 ? u + 2 * step : u, p);
@@ -938,7 +938,9 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
       float* dst1 = dst0 + 8 * kHeadDim;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
-        float acc[4] = {pg * c[n][0], pg * c[n][1], pg * c[n][2], pg * c[n][3]};
+        const float2 s01 = __fmul2_rn(make_float2(c[n][0], c[n][1]), make_float2(pg, pg));
+        const float2 s23 = __fmul2_rn(make_float2(c[n][2], c[n][3]), make_float2(pg, pg));
+        float acc[4] = {s01.x, s01.y, s23.x, s23.y};
         const uint32_t b0 = __float_as_uint(krow[8 * n + g8]);
         mma_16x8x8_tf32(acc, ch0, ch1, 0u, 0u, b0, 0u);
         mma_16x8x8_tf32(acc, cl0, cl1, 0u, 0u, b0, 0u);
