@@ -580,7 +580,7 @@ __global__ void __launch_bounds__(kPipeWarps * 32, 4) decode_mtp_pipe_kernel(Dec
 // one.  The state crosses HBM once per call; each unit's rows (into padded
 // shared rows, so the fragment loads are free of bank conflicts) and token rows
 // are bulk-copied one unit ahead.
-constexpr int kChunkMaxT = 4;
+constexpr int kChunkMaxT = 8;
 constexpr int kChunkWarps = 4;
 
 // Enumeration of the Gram scalars of T tokens (vectors w < T are k_w, w >= T are
@@ -589,8 +589,9 @@ constexpr int kChunkWarps = 4;
 template <int T, bool L2NORM>
 struct ChunkGram {
   static constexpr int kDots = T * T + (L2NORM ? 2 * T : 0);
-  static constexpr int kPad = kDots <= 1 ? 1 : kDots <= 2 ? 2 : kDots <= 4 ? 4 : kDots <= 8 ? 8 : kDots <= 16 ? 16 : 32;
-  static_assert(kDots <= 32, "Gram scalars of at most 32");
+  // up to 32: one power-of-two reduce-scatter; beyond: batches of 32
+  static constexpr int kPad = kDots <= 1 ? 1 : kDots <= 2 ? 2 : kDots <= 4 ? 4 : kDots <= 8 ? 8 : kDots <= 16 ? 16
+                            : (kDots + 31) / 32 * 32;
   static constexpr int kk(int j, int t) { return t * t + j; }
   static constexpr int kq(int j, int t) { return t * t + t + j; }
   static constexpr int nk(int t) { return T * T + t; }
@@ -645,6 +646,8 @@ constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n / 2); }
 constexpr int kChunkRows = 16;
 constexpr uint32_t kChunkRowBytes = kChunkRows * kHeadDim * 4;  // 8192
 constexpr int kPadRow = kHeadDim + 8;                           // padded shared row (floats): 544 B
+// token vectors (k_0 .., q_0 ..) in tiles of 8 (the N of one mma): one tile up to 4 tokens, two up to 8
+__host__ __device__ constexpr int chunk_vec_tiles(int T) { return (2 * T + 7) / 8; }
 // token rows of a unit: q and k (256 B each) per token, then v of the unit's 16 rows (32 B) per token
 __host__ __device__ constexpr uint32_t chunk_tok_bytes(int T) { return (uint32_t)T * (2 * kHeadDim * 2 + kChunkRows * 2); }
 // per token in shared memory: v of the 16 rows, g, beta (fp32)
@@ -652,9 +655,9 @@ constexpr int kChunkScal = kChunkRows + 2;
 
 template <int T, bool L2NORM>
 __host__ __device__ constexpr uint32_t chunk_warp_bytes() {
-  // rows [16][kPadRow] fp32 | token rows | q, k widened [8][kPadRow] fp32 (rows >= 2T zero) |
-  // Gram scalars | per-token scalars | 2 mbarriers
-  return (uint32_t)(kChunkRows * kPadRow * 4) + chunk_tok_bytes(T) + (uint32_t)(8 * kPadRow * 4) +
+  // rows [16][kPadRow] fp32 | token rows | q, k widened [8 x vector tiles][kPadRow] fp32 (rows >= 2T
+  // zero) | Gram scalars | per-token scalars | 2 mbarriers
+  return (uint32_t)(kChunkRows * kPadRow * 4) + chunk_tok_bytes(T) + (uint32_t)(8 * chunk_vec_tiles(T) * kPadRow * 4) +
          ChunkGram<T, L2NORM>::kBytes + (uint32_t)((T * kChunkScal * 4 + 15) / 16 * 16) + 16;
 }
 
@@ -688,16 +691,17 @@ __device__ __forceinline__ void mma_16x8x8_tf32(float (&d)[4], uint32_t a0, uint
 }
 
 template <int T, bool L2NORM>
-__global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(DecodeMtpParams p) {
+__global__ void __launch_bounds__(kChunkWarps * 32, T > 4 ? 2 : 3) decode_mtp_chunk_kernel(DecodeMtpParams p) {
   using G = ChunkGram<T, L2NORM>;
+  constexpr int NV = chunk_vec_tiles(T);  // 8-vector tiles of W
   constexpr uint32_t kTok = chunk_tok_bytes(T);
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* wbase = smem_raw + (size_t)warp * chunk_warp_bytes<T, L2NORM>();
   float* rows_buf = reinterpret_cast<float*>(wbase);  // [16][kPadRow]
   unsigned char* tok_buf = wbase + kChunkRows * kPadRow * 4;
-  float* qk32 = reinterpret_cast<float*>(tok_buf + kTok);  // [8][kPadRow]: k_0 .. k_{T-1}, q_0 .. q_{T-1}, 0 ..
-  float* gram = qk32 + 8 * kPadRow;
+  float* qk32 = reinterpret_cast<float*>(tok_buf + kTok);  // [8 NV][kPadRow]: k_0 .. k_{T-1}, q_0 .. q_{T-1}, 0 ..
+  float* gram = qk32 + 8 * NV * kPadRow;
   float* scal = gram + G::kBytes / 4;  // [T][kChunkScal]: v of rows 0-15, g, beta
   uint64_t* bars = reinterpret_cast<uint64_t*>(
       reinterpret_cast<unsigned char*>(scal) + (T * kChunkScal * 4 + 15) / 16 * 16);  // rows, tokens
@@ -713,7 +717,7 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
     fence_barrier_init();
   }
   // the zero padding vectors (w >= 2T) of W, written once
-  for (int e = lane; e < (8 - 2 * T) * kPadRow; e += 32) qk32[2 * T * kPadRow + e] = 0.f;
+  for (int e = lane; e < (8 * NV - 2 * T) * kPadRow; e += 32) qk32[2 * T * kPadRow + e] = 0.f;
   __syncwarp();
 
   auto issue_rows = [&](const PipeItem& it, int64_t slot) {
@@ -808,7 +812,7 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
       issue_tok(nx);
       ++tok_issued;
     }
-    {
+    if constexpr (G::kPad <= 32) {
       float gp[G::kPad];
 #pragma unroll
       for (int d = 0; d < G::kPad; ++d) {
@@ -820,12 +824,28 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
         }
       }
       WarpReduceScatter<G::kPad, 16>::run(gp, lane);
-      if constexpr (G::kPad >= 32) {
-#pragma unroll
-        for (int i = 0; i < G::kPad / 32; ++i) gram[lane * (G::kPad / 32) + i] = gp[i];
+      if constexpr (G::kPad == 32) {
+        gram[lane] = gp[0];
       } else {
         constexpr int sh = 5 - ilog2(G::kPad);
         if ((lane & ((1 << sh) - 1)) == 0) gram[lane >> sh] = gp[0];
+      }
+    } else {
+#pragma unroll
+      for (int b0 = 0; b0 < G::kPad; b0 += 32) {  // 32 scalars per batch, lane l keeps scalar b0 + l
+        float gp[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int d = b0 + i;
+          if (d < G::kDots) {
+            const float4 x = wv[G::va(d)], y = wv[G::vb(d)];
+            gp[i] = fmaf(x.x, y.x, fmaf(x.y, y.y, fmaf(x.z, y.z, x.w * y.w)));
+          } else {
+            gp[i] = 0.f;
+          }
+        }
+        WarpReduceScatter<32, 16>::run(gp, lane);
+        gram[b0 + lane] = gp[0];
       }
     }
 
@@ -857,8 +877,9 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
         out_unit[(size_t)(e >> 4) * p.o_st + (e & 15)] = __float2bfloat16_rn(0.f);
     } else {
       // ---- A: D = S W (rows g8, g8 + 8 of the unit; token vectors 2 t4, 2 t4 + 1) ----
-      // four independent accumulators (hi / lo x even / odd steps) keep the mma chains short
-      float da[4][4] = {};
+      // per vector tile, four independent accumulators (hi / lo x even / odd steps) keep the
+      // mma chains short
+      float da[NV][4][4] = {};
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         uint32_t ah[4], al[4];
@@ -866,23 +887,29 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
         tf32_split(c[n][2], ah[1], al[1]);  // (g8 + 8, t4)
         tf32_split(c[n][1], ah[2], al[2]);  // (g8, t4 + 4)
         tf32_split(c[n][3], ah[3], al[3]);  // (g8 + 8, t4 + 4)
-        const float2 bw = *reinterpret_cast<const float2*>(qk32 + g8 * kPadRow + 8 * n + 2 * t4);  // vector g8
-        const uint32_t b0 = __float_as_uint(bw.x), b1 = __float_as_uint(bw.y);
-        mma_16x8x8_tf32(da[2 * (n & 1)], ah[0], ah[1], ah[2], ah[3], b0, b1);
-        mma_16x8x8_tf32(da[2 * (n & 1) + 1], al[0], al[1], al[2], al[3], b0, b1);
+#pragma unroll
+        for (int vt = 0; vt < NV; ++vt) {  // vector 8 vt + g8
+          const float2 bw = *reinterpret_cast<const float2*>(qk32 + (8 * vt + g8) * kPadRow + 8 * n + 2 * t4);
+          const uint32_t b0 = __float_as_uint(bw.x), b1 = __float_as_uint(bw.y);
+          mma_16x8x8_tf32(da[vt][2 * (n & 1)], ah[0], ah[1], ah[2], ah[3], b0, b1);
+          mma_16x8x8_tf32(da[vt][2 * (n & 1) + 1], al[0], al[1], al[2], al[3], b0, b1);
+        }
       }
-      float dacc[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) dacc[i] = (da[0][i] + da[2][i]) + (da[1][i] + da[3][i]);
       // every lane of the quad gathers all 2T products of rows g8 and g8 + 8
-      float x[2][8];
+      float x[2][8 * NV];
 #pragma unroll
-      for (int tq = 0; tq < 4; ++tq) {
-        const int src = (lane & ~3) | tq;
-        x[0][2 * tq] = __shfl_sync(0xffffffffu, dacc[0], src);
-        x[0][2 * tq + 1] = __shfl_sync(0xffffffffu, dacc[1], src);
-        x[1][2 * tq] = __shfl_sync(0xffffffffu, dacc[2], src);
-        x[1][2 * tq + 1] = __shfl_sync(0xffffffffu, dacc[3], src);
+      for (int vt = 0; vt < NV; ++vt) {
+        float dacc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dacc[i] = (da[vt][0][i] + da[vt][2][i]) + (da[vt][1][i] + da[vt][3][i]);
+#pragma unroll
+        for (int tq = 0; tq < 4; ++tq) {
+          const int src = (lane & ~3) | tq;
+          x[0][8 * vt + 2 * tq] = __shfl_sync(0xffffffffu, dacc[0], src);
+          x[0][8 * vt + 2 * tq + 1] = __shfl_sync(0xffffffffu, dacc[1], src);
+          x[1][8 * vt + 2 * tq] = __shfl_sync(0xffffffffu, dacc[2], src);
+          x[1][8 * vt + 2 * tq + 1] = __shfl_sync(0xffffffffu, dacc[3], src);
+        }
       }
       // ---- B: the token recurrence on scalars for rows g8 (ps 0) and g8 + 8 (ps 1) ----
       float nkv[T], nqv[T];  // 1 / |k_t|, 1 / |q_t| with the L2 norm, else 1
@@ -892,7 +919,7 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
         nqv[t] = L2NORM ? rsqrtf(gram[G::nq(t)] + 1e-6f) : 1.f;
       }
       const float scale = p.scale;
-      float cm[2], pg = 1.f;  // cm: c of token t4 for the lane's two rows; pg = prod g
+      float cm[2][2], pg = 1.f;  // cm[ps][h]: c of token t4 + 4 h for the lane's two rows; pg = prod g
 #pragma unroll
       for (int t = 0; t < T; ++t) pg *= scal[t * kChunkScal + kChunkRows];
 #pragma unroll
@@ -904,13 +931,13 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
           z[T + t] = x[ps][T + t] * nqv[t];
         }
         const int vr = g8 + 8 * ps;
-        float dl[T], om = 0.f;  // om: the output of token t4 (this lane's store)
+        float dl[T], om[2] = {0.f, 0.f};  // om[h]: the output of token t4 + 4 h (this lane's stores)
 #pragma unroll
         for (int t = 0; t < T; ++t) {
           const float g = scal[t * kChunkScal + kChunkRows];
           const float d = scal[t * kChunkScal + kChunkRows + 1] * (scal[t * kChunkScal + vr] - g * z[t]);
           const float o = scale * fmaf(d, gram[G::kq(t, t)] * (nkv[t] * nqv[t]), g * z[T + t]);
-          om = t4 == t ? o : om;
+          if ((t & 3) == t4) om[t >> 2] = o;
           dl[t] = d;
 #pragma unroll
           for (int t2 = t + 1; t2 < T; ++t2) {
@@ -919,20 +946,25 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
           }
         }
         float tail = 1.f;  // prod_{i > j} g_i
-        cm[ps] = 0.f;
+        cm[ps][0] = cm[ps][1] = 0.f;
 #pragma unroll
         for (int t = T - 1; t >= 0; --t) {
           const float cj = dl[t] * tail * nkv[t];
-          cm[ps] = t4 == t ? cj : cm[ps];
+          if ((t & 3) == t4) cm[ps][t >> 2] = cj;
           tail *= scal[t * kChunkScal + kChunkRows];
         }
-        if (t4 < T) out_unit[(size_t)t4 * p.o_st + vr] = __float2bfloat16_rn(om);  // token t4's output
+        if (t4 < T) out_unit[(size_t)t4 * p.o_st + vr] = __float2bfloat16_rn(om[0]);  // token t4's output
+        if (t4 + 4 < T) out_unit[(size_t)(t4 + 4) * p.o_st + vr] = __float2bfloat16_rn(om[1]);  // token t4 + 4
       }
-      // ---- C: S <- (prod g) S + C K: A = c (rows g8, g8 + 8; token t4 < T, else 0), B = k_t4 ----
-      uint32_t ch0, cl0, ch1, cl1;
-      tf32_split(cm[0], ch0, cl0);
-      tf32_split(cm[1], ch1, cl1);
-      const float* krow = qk32 + (t4 < T ? t4 : 2 * T) * kPadRow;  // k_t4, or a zero row
+      // ---- C: S <- (prod g) S + C K: A = c (rows g8, g8 + 8; tokens t4 and t4 + 4, 0 beyond T),
+      //      B = k_t4, k_{t4 + 4} (0 beyond T) ----
+      uint32_t ch[4], cl[4];
+      tf32_split(cm[0][0], ch[0], cl[0]);  // (g8, t4)
+      tf32_split(cm[1][0], ch[1], cl[1]);  // (g8 + 8, t4)
+      tf32_split(cm[0][1], ch[2], cl[2]);  // (g8, t4 + 4)
+      tf32_split(cm[1][1], ch[3], cl[3]);  // (g8 + 8, t4 + 4)
+      const float* krow0 = qk32 + (t4 < T ? t4 : 0) * kPadRow;
+      const float* krow1 = qk32 + (t4 + 4 < T ? t4 + 4 : 0) * kPadRow;
       float* dst0 = p.new_pool + (size_t)slot * p.n_sn + (size_t)it.h * p.n_sh + (size_t)(it.wrow0 + g8) * kHeadDim +
                     2 * t4;
       float* dst1 = dst0 + 8 * kHeadDim;
@@ -941,9 +973,10 @@ __global__ void __launch_bounds__(kChunkWarps * 32, 3) decode_mtp_chunk_kernel(D
         const float2 s01 = __fmul2_rn(make_float2(c[n][0], c[n][1]), make_float2(pg, pg));
         const float2 s23 = __fmul2_rn(make_float2(c[n][2], c[n][3]), make_float2(pg, pg));
         float acc[4] = {s01.x, s01.y, s23.x, s23.y};
-        const uint32_t b0 = __float_as_uint(krow[8 * n + g8]);
-        mma_16x8x8_tf32(acc, ch0, ch1, 0u, 0u, b0, 0u);
-        mma_16x8x8_tf32(acc, cl0, cl1, 0u, 0u, b0, 0u);
+        const uint32_t b0 = t4 < T ? __float_as_uint(krow0[8 * n + g8]) : 0u;
+        const uint32_t b1 = t4 + 4 < T ? __float_as_uint(krow1[8 * n + g8]) : 0u;
+        mma_16x8x8_tf32(acc, ch[0], ch[1], ch[2], ch[3], b0, b1);
+        mma_16x8x8_tf32(acc, cl[0], cl[1], cl[2], cl[3], b0, b1);
         __stcs(reinterpret_cast<float2*>(dst0 + 8 * n), make_float2(acc[0], acc[1]));
         __stcs(reinterpret_cast<float2*>(dst1 + 8 * n), make_float2(acc[2], acc[3]));
       }
@@ -1047,11 +1080,15 @@ cudaError_t launch_chunk(const DecodeMtpParams& p, cudaStream_t stream) {
 
 template <bool L2NORM>
 cudaError_t launch_chunk_any(const DecodeMtpParams& p, cudaStream_t stream) {
-  static_assert(kChunkMaxT == 4, "one instantiation per token count");
+  static_assert(kChunkMaxT == 8, "one instantiation per token count");
   switch (p.T) {
     case 2: return launch_chunk<2, L2NORM>(p, stream);
     case 3: return launch_chunk<3, L2NORM>(p, stream);
     case 4: return launch_chunk<4, L2NORM>(p, stream);
+    case 5: return launch_chunk<5, L2NORM>(p, stream);
+    case 6: return launch_chunk<6, L2NORM>(p, stream);
+    case 7: return launch_chunk<7, L2NORM>(p, stream);
+    case 8: return launch_chunk<8, L2NORM>(p, stream);
   }
   return cudaErrorInvalidValue;
 }

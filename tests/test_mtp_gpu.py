@@ -165,9 +165,9 @@ def test_index_beyond_pool_sets_device_error(gdn):
     assert not out[1].float().abs().any()
 
 
-@pytest.mark.parametrize("T,l2", [(2, False), (2, True), (3, True), (4, False), (4, True)])
+@pytest.mark.parametrize("T,l2", [(2, False), (2, True), (3, True), (4, False), (4, True), (5, False), (6, True), (7, False), (8, False), (8, True)])
 def test_chunked_tokens_match_token_serial_kernel(gdn, T, l2):
-    """2 to 4 tokens without intermediate states run the chunked kernel (every token's
+    """2 to 8 tokens without intermediate states run the chunked kernel (every token's
     products with the state from the item's initial rows, the token recurrence on
     scalars through the Gram matrix of q and k); a call that also asks for the
     intermediate states runs the token-serial kernel.  Both must give the same outputs
