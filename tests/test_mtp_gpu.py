@@ -60,7 +60,7 @@ def test_golden_flashinfer_mtp_reference(gdn):
     assert torch.equal(fin[0], pool[0]) and torch.equal(fin[2], pool[2])  # untouched slots
 
 
-@pytest.mark.parametrize("T", [1, 4, 8, 19])  # <= 8: warp-pipelined kernel; 19: two token groups
+@pytest.mark.parametrize("T", [1, 4, 8, 19])  # 1: single-token kernel; 4, 8: chunked; 19: general kernel, two token groups
 def test_random_pool_with_padding_entry(gdn, T):
     d = mtp_inputs(gdn, B=5, T=T, P=8, seed=200 + T)
     idx = [6, -1, 0, 3, 7]
