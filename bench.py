@@ -17,7 +17,8 @@ clock record): ``decode_b1024`` = configs[2] (1024 sequences split over the N
 ranks, strong scaling), ``prefill`` = configs[3] (varlen, 16 sequences, on every
 rank), ``prefill_8x32768`` = configs[4] (8 x 32768 tokens split over the ranks by
 sequence, strong scaling), ``mtp`` = pooled multi-token decode (64 sequences x 4
-tokens, in-place state pool).  At N = 1 rank 0 also times the CPU baselines (the
+tokens, in-place state pool; ``--workload mtp_b64_t4`` adds the same call at 1 .. 8
+tokens per sequence as ``tokens_sweep``).  At N = 1 rank 0 also times the CPU baselines (the
 C restatement of the reference recurrence for decode and prefill, and the
 flashinfer torch reference recurrence) and ``reference_triton``: the reference's
 own Triton kernels (``solution/triton/kernel_{decode,prefill}.py::run``,
@@ -756,6 +757,18 @@ def run_ours(args, world, rank, local):
                              "avg_launch_us": mlaunch * 1e3, "algorithmic_bytes_per_launch": mbytes},
                 "clocks": sampler_m.summary()}
         if wl == "mtp_b64_t4":
+            # the same call at 1 .. 8 tokens per sequence (T = 1 is the single-token kernel on the
+            # indexed slots, 2 .. 8 the chunked kernel)
+            sweep = {}
+            for tt in range(1, 9):
+                tsets = msets if tt == mt else mtp_sets(gdn, mb, tt, 3, seed=rank + 7, device="cuda")
+                tms, tlaunch = time_steps(lambda s: mtp_call(gdn, s), tsets, msteps, mwarm, world, None, graph=True)
+                tbytes = gdn.workloads.mtp_bytes_per_seq(tt) * mb
+                sweep[str(tt)] = {"us_per_call": tlaunch * 1e3, "gbs": tbytes / (tlaunch * 1e-3) / 1e9,
+                                  "frac": tbytes / (tlaunch * 1e-3) / 1e9 / hbm_peak}
+                if tsets is not msets:
+                    del tsets
+            mres["tokens_sweep"] = sweep
             result.update(metric="GDN multi-token decode state GB/s", value=mres["gbs"], unit="GB/s",
                           ms_per_step=mms, dtype="f32",
                           config={"workload": wl, "batch_per_rank": mb, "tokens_per_seq": mt,
