@@ -196,16 +196,12 @@ def prefill_sets(gdn, seqlens, n_sets, seed, device, zero_state=False):
 
 def prefill_launches(gdn, seqlens):
     """Kernels one prefill step launches: prep + chain, or with the automatic in-GPU
-    segments prep + pass 1 (+ the map composition for 3 or more segments) + reruns.
-    The segment count is read off the workspace size, whose extra part is one fp32
-    state per (sequence, v-head) for 2 segments and 3 S - 5 of them for S >= 3."""
+    segments prep + pass 1 (segment 0 and the later segments' maps) + the map
+    composition + the output correction; segments show as extra workspace."""
     N, T = len(seqlens), sum(seqlens)
     auto = gdn.kernel_prefill.workspace_size(N, T, 16, 32)
     one = gdn.kernel_prefill.workspace_size(N, T, 16, 32, segments=1)
-    if auto <= one:
-        return 2
-    per_state = N * 32 * 128 * 128 * 4
-    return 4 if (auto - one) >= 2 * per_state else 3
+    return 2 if auto <= one else 4
 
 
 def prefill_call(gdn, s, use_qk_l2norm=False):

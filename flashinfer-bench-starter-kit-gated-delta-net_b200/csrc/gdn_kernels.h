@@ -66,11 +66,16 @@ struct PrefillParams {
   void* workspace;
   size_t workspace_bytes;
   // context parallelism inside the GPU (set by the chunked launcher): each sequence's
-  // chunks split into cp_segments ranges; cp_pass 0 = one chain per sequence, 1 = the
-  // segment maps, 3 = the segment reruns; cp_scratch = segment states and maps
+  // chunks split into cp_segments ranges (segment 0 takes cp_w0 / 1024 of them);
+  // cp_pass 0 = one chain per sequence, 1 = segment 0 and the maps and homogeneous
+  // outputs of the others; cp_scratch = segment states and maps, cp_phi = the
+  // homogeneous outputs [T][HV][128]
   int cp_segments = 1;
   int cp_pass = 0;
+  int cp_w0 = 0;
+  int cp_parts = 1;  // output correction: CTAs per segment (each a contiguous part of its chunks)
   float* cp_scratch = nullptr;
+  __nv_bfloat16* cp_phi = nullptr;
   // GDN_FLAG_QK_L2NORM: per (token, q/k head) (1 / |q|, log2 (1 / |q|)), [T][HQ] (workspace)
   float2* qnorm = nullptr;
   // cp_pass 2: each sequence's affine state map S_out = S_in M + C instead of a prefill

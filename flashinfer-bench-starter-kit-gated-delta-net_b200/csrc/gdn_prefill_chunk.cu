@@ -48,6 +48,13 @@
 // loop, then in-flight copies and MMAs are drained before TMEM is freed.
 #include <cuda.h>
 
+#include <functional>
+#include <map>
+#include <mutex>
+#include <queue>
+#include <utility>
+#include <vector>
+
 #include "gdn_prefill_chunk.cuh"
 
 namespace gdn {
@@ -142,7 +149,7 @@ struct Smem {
 // blocking tests (the hardware suspends the thread until the phase completes or
 // a short time limit passes, so a waiting thread takes no issue slots), then
 // tests with a longer suspend hint between abort and time-limit checks.
-__device__ __forceinline__ bool wait_bar(const Smem& sm, uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool wait_bar_flag(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const uint32_t addr = smem_u32(bar);
 #pragma unroll 1
   for (int k = 0; k < 64; ++k)
@@ -153,13 +160,16 @@ __device__ __forceinline__ bool wait_bar(const Smem& sm, uint64_t* bar, uint32_t
     // suspended until the phase completes (or 0.1 ms), so waiting threads do not
     // take issue slots from the warps doing the work
     if (mbar_try_wait_sleep(addr, parity, 100000u)) return true;
-    if (*sm.abort_flag()) return false;
+    if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       raise_device_error(kDevErrWaitTimeout);
-      *sm.abort_flag() = 1;
+      *abort_flag = 1;
       return false;
     }
   }
+}
+__device__ __forceinline__ bool wait_bar(const Smem& sm, uint64_t* bar, uint32_t parity) {
+  return wait_bar_flag(bar, parity, sm.abort_flag());
 }
 
 // Longest chains first.  CTAs start in blockIdx order, so blockIdx.y is mapped to
@@ -213,7 +223,7 @@ __device__ __forceinline__ bool group_wait(const Smem& sm, int bar_idx, uint32_t
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_chunk_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapQ,
                          const __grid_constant__ CUtensorMap mapV, const __grid_constant__ CUtensorMap mapO,
-                         PrefillParams p) {
+                         const __grid_constant__ CUtensorMap mapPhi, PrefillParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   Smem sm;
   sm.base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -231,19 +241,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- this CTA's task: a chunk range of the sequence, where its state starts and ends ----
   // cp_pass 0: the whole sequence from p.state to p.new_state, with outputs.
   // cp_pass 1 (z): 0 = segment 0 from p.state, with outputs, its final state -> kCpIn[0];
-  //   2 s - 1 = M of segment s (identity start, v taken as 0), 2 s = C of segment s
-  //   (zero start), no outputs (s = 1 .. S - 2).
-  // cp_pass 3 (z): segment z + 1 from kCpIn[z], with outputs; the last one ends in p.new_state.
+  //   2 s - 1 = M of segment s (identity start, v taken as 0), its outputs (the homogeneous
+  //   outputs Phi) -> p.cp_phi, final state -> kCpMap[s - 1];
+  //   2 s = C of segment s (zero start), its outputs -> p.out (corrected later by
+  //   S_in Phi), final state -> kCpOff[s - 1]   (s = 1 .. S - 1).
   // cp_pass 2 (z): the sequence's map, no outputs: z = 2 s -> M, 2 s + 1 -> C of segment s;
   //   one segment: straight to p.map_m / p.map_c, else to the map scratch (composed later).
   const int S = p.cp_segments, cz = blockIdx.z;
-  const int seg = p.cp_pass == 1 ? (cz + 1) >> 1 : (p.cp_pass == 3 ? cz + 1 : (p.cp_pass == 2 ? cz >> 1 : 0));
-  const bool emit = p.cp_pass == 0 || p.cp_pass == 3 || (p.cp_pass == 1 && cz == 0);  // outputs written
-  const bool homog = (p.cp_pass == 1 && (cz & 1)) || (p.cp_pass == 2 && !(cz & 1));   // identity start, v = 0
+  const int seg = p.cp_pass == 1 ? (cz + 1) >> 1 : (p.cp_pass == 2 ? cz >> 1 : 0);
+  const bool emit = p.cp_pass == 0 || p.cp_pass == 1;                                // outputs written
+  const bool homog = (p.cp_pass == 1 && (cz & 1)) || (p.cp_pass == 2 && !(cz & 1));  // identity start, v = 0
   // where the range's state starts (nullptr: zero, or the identity when homog) and ends
   // (nullptr: not stored); evaluated where used, to keep them out of the loops' registers
   auto init_block = [&]() -> const float* {
-    if (p.cp_pass == 3) return p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, seg - 1, h);
     if ((p.cp_pass == 1 && cz != 0) || p.cp_pass == 2) return nullptr;
     return p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh : nullptr;
   };
@@ -251,7 +261,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.cp_pass == 1)
       return p.cp_scratch + (cz == 0 ? cp_offset(p.N, p.HV, S, kCpIn, n, 0, h)
                                      : cp_offset(p.N, p.HV, S, (cz & 1) ? kCpMap : kCpOff, n, seg - 1, h));
-    if (p.cp_pass == 3 && seg != S - 1) return nullptr;
     if (p.cp_pass == 2) {
       if (S > 1) return p.cp_scratch + map_seg_offset(p.N, p.HV, S, cz & 1, n, seg, h);
       return !(cz & 1) ? p.map_m + (size_t)n * p.m_sn + (size_t)h * p.m_sh : p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh;
@@ -259,7 +268,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     return p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh;
   };
   const int nch_seq = (int)((seq_len + kC - 1) / kC);
-  const int cb = (int)((int64_t)seg * nch_seq / S), ce = (int)((int64_t)(seg + 1) * nch_seq / S);
+  int cb = 0, ce = nch_seq;
+  if (p.cp_pass == 1) {
+    segment_range(nch_seq, S, p.cp_w0, seg, cb, ce);
+  } else if (p.cp_pass == 2) {
+    cb = (int)((int64_t)seg * nch_seq / S);
+    ce = (int)((int64_t)(seg + 1) * nch_seq / S);
+  }
   const int64_t t0 = cu0 + (int64_t)cb * kC;  // first token of the range
   const int64_t len = ce > cb ? (seq_len < (int64_t)ce * kC ? seq_len : (int64_t)ce * kC) - (int64_t)cb * kC : 0;
   const int nchunks = ce - cb;
@@ -311,6 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::prefetch_tensormap(&mapQ);
         tc::prefetch_tensormap(&mapV);
         tc::prefetch_tensormap(&mapO);
+        if (homog && emit) tc::prefetch_tensormap(&mapPhi);
       }
       int issued = 0;
       for (int i = 0; i < nchunks; ++i) {
@@ -501,12 +517,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_proxy_async_smem();
       named_sync(2, 128);
       if (warp == kWarpP0 && emit) {
+        // a pass-1 homogeneous chain writes Phi ([T][HV][128], rows contiguous) instead of out
+        const bool to_phi = homog;
         if (nvalid == kC) {  // whole chunk: one tiled store of the [64 x 128] box
-          if (lane == 0) tc::tma_store_3d(&mapO, 0, h, (int)(t0 + (int64_t)ci * kC), ostage);
+          if (lane == 0) tc::tma_store_3d(to_phi ? &mapPhi : &mapO, 0, h, (int)(t0 + (int64_t)ci * kC), ostage);
         } else {  // a sequence's last, partial chunk: only its own rows
-          __nv_bfloat16* out = p.out + (t0 + (int64_t)ci * kC) * p.o_st + (int64_t)h * p.o_sh;
+          const int64_t ost = to_phi ? (int64_t)p.HV * kHeadDim : p.o_st;
+          __nv_bfloat16* out = (to_phi ? p.cp_phi : p.out) + (t0 + (int64_t)ci * kC) * ost +
+                               (int64_t)h * (to_phi ? (int64_t)kHeadDim : p.o_sh);
           for (int t = lane; t < nvalid; t += 32)
-            tc::bulk_s2g(out + (int64_t)t * p.o_st, ostage + t * kHeadDim, 256);
+            tc::bulk_s2g(out + (int64_t)t * ost, ostage + t * kHeadDim, 256);
         }
         tc::bulk_commit();
       }
@@ -821,9 +841,10 @@ bool make_map(CUtensorMap* m, const void* base, int64_t tokens, int heads, int64
 }
 
 // Composition of the segment state maps (context parallelism inside the GPU):
-// S_in(s + 1) = S_in(s) M_s + C_s for s = 1 .. S - 2, fp32 on the CUDA cores.  The
-// state rows are independent under the maps, so a CTA carries its 32 rows of one
-// (sequence, v-head) through every step without synchronising with other CTAs.
+// S_in(s + 1) = S_in(s) M_s + C_s for s = 1 .. S - 1, fp32 on the CUDA cores; S_in(S) is
+// the sequence's final state (new_state).  The state rows are independent under the maps,
+// so a CTA carries its 32 rows of one (sequence, v-head) through every step without
+// synchronising with other CTAs.
 __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
   __shared__ __align__(16) float rows[32][kHeadDim];
   const int h = blockIdx.x, n = blockIdx.y, r0 = blockIdx.z * 32;
@@ -833,7 +854,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
   for (int e = tid; e < 32 * kHeadDim / 4; e += 256)
     reinterpret_cast<float4*>(&rows[0][0])[e] = reinterpret_cast<const float4*>(in1)[e];
   __syncthreads();
-  for (int sg = 1; sg <= S - 2; ++sg) {
+  for (int sg = 1; sg <= S - 1; ++sg) {
     const float* M = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpMap, n, sg - 1, h);
     const float* C = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpOff, n, sg - 1, h) + (int64_t)r0 * kHeadDim;
     float acc[16];
@@ -853,13 +874,229 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
       }
     }
     __syncthreads();  // every thread has read the rows of S_in(sg)
-    float* out = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, sg, h) + (int64_t)r0 * kHeadDim;
+    float* out = (sg < S - 1 ? p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, sg, h)
+                             : p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh) +
+                 (int64_t)r0 * kHeadDim;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       rows[rh + r][c] = acc[r];
       out[(rh + r) * kHeadDim + c] = acc[r];
     }
     __syncthreads();
+  }
+}
+
+// Output correction of the context-parallel segments (after pass 1 and the map
+// composition, cp_segments >= 2).  Every (sequence, v-head) state evolves affinely in its
+// initial state, and so do the outputs: for a token t of segment s >= 1,
+//   o_t = o_t(zero initial state) + S_in(s) Phi_t,
+// with Phi_t the output of the segment's homogeneous chain (run from the identity, v = 0).
+// Pass 1 wrote the first term to out and Phi to p.cp_phi; this kernel adds the second:
+//   out[t][v] += sum_j S_in(s)[v][j] Phi[t][j].
+// tcgen05: D [128 v x 64 tokens] = S_in [128 v x 128 j] Phi^T per chunk, S_in split into
+// bf16 hi + lo (two products) and held in TMEM as the A operand, Phi from shared memory,
+// fp32 accumulation in TMEM (two 64-column buffers).  256 TMEM columns and 97 KB of shared
+// memory per CTA, so two CTAs share an SM.
+// CTA = (v-head, sequence, segment - 1 and a part of its chunks: grid z = (S - 1) x
+// p.cp_parts), looping over those chunks; 6 warps:
+//   0-3  thread = state row v: S_in hi / lo into TMEM (while the first loads are in
+//        flight), then per chunk D from TMEM added to the out tile in shared memory,
+//        which is stored back (TMA)
+//   4    TMA loads of the Phi tile and the out tile, kStages deep
+//   5    TMEM allocation and the MMA issue
+namespace corr {
+constexpr int kThreads = 192;
+constexpr int kStages = 3;            // shared-memory stages (Phi tile | out tile)
+constexpr int kDBufs = 2;             // TMEM accumulators
+constexpr uint32_t kSmStage = 0;      // kStages x (Phi chunk: 2 SW128 tiles [64 tokens x 64 j], 8 KB each |
+constexpr uint32_t kStageBytes = 32768;  //            out tile [64 tokens][128 v] bf16, plain, 16 KB)
+constexpr uint32_t kOOff = 16384;
+constexpr uint32_t kSmBar = kSmStage + kStages * kStageBytes;
+constexpr uint32_t kSmMisc = kSmBar + 128;
+constexpr uint32_t kSmBytes = kSmMisc + 32;
+constexpr uint32_t kSmAlloc = kSmBytes + 1024;
+constexpr uint32_t kTmemCols = 256;   // A hi [0, 64), A lo [64, 128) (bf16 pairs), D buffers [128, 256)
+constexpr uint32_t kTmAhi = 0, kTmAlo = 64, kTmD = 128;
+enum : int {
+  B_FULL = 0,                    // [kStages] Phi and out tiles landed
+  B_EMPTY = kStages,             // [kStages] the stage's out tile has been read by its store
+  B_MMA = 2 * kStages,           // [kDBufs] D of a chunk complete
+  B_TFREE = 2 * kStages + kDBufs,  // [kDBufs] the epilogue has read a D buffer
+  B_AREADY = 2 * kStages + 2 * kDBufs,
+  B_DRAIN,
+  B_COUNT
+};
+static_assert(B_COUNT * 8 <= 128 && kTmD + kDBufs * 64 <= kTmemCols && 2 * (kSmAlloc + 1024) <= 232448, "layout");
+}  // namespace corr
+
+__global__ void __launch_bounds__(corr::kThreads, 2)
+    prefill_correct_kernel(const __grid_constant__ CUtensorMap mapPhi, const __grid_constant__ CUtensorMap mapO,
+                           PrefillParams p) {
+  using corr::kDBufs;
+  using corr::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int parts = p.cp_parts;
+  const int h = blockIdx.x, n = blockIdx.y, seg = (int)blockIdx.z / parts + 1, part = (int)blockIdx.z % parts;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = p.cp_segments;
+  const int64_t cu0 = load_cu(p, n), cu1 = load_cu(p, n + 1);
+  const bool bad = cu1 < cu0 || cu0 < 0 || cu1 > p.T;
+  const int64_t seq_len = bad ? 0 : cu1 - cu0;
+  int sb = 0, se = 0;
+  segment_range((int)((seq_len + kC - 1) / kC), S, p.cp_w0, seg, sb, se);
+  const int cb = sb + (se - sb) * part / parts, ce = sb + (se - sb) * (part + 1) / parts;
+  const int nchunks = ce - cb;
+  if (nchunks <= 0) return;  // the same for every thread of the CTA, before any barrier
+  const int64_t t0 = cu0 + (int64_t)cb * kC;
+  const int64_t len = (seq_len < (int64_t)ce * kC ? seq_len : (int64_t)ce * kC) - (int64_t)cb * kC;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + corr::kSmBar);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + corr::kSmMisc + 16);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + corr::kSmMisc);
+
+  if (tid == 0) {
+    for (int i = 0; i < corr::B_COUNT; ++i) mbar_init(&bar[i], i == corr::B_AREADY ? 4 : 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(tmem_slot, corr::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---- TMA: Phi tile (two 64-column SW128 boxes) and the out tile of each chunk ----
+    if (lane == 0) {
+      tc::prefetch_tensormap(&mapPhi);
+      tc::prefetch_tensormap(&mapO);
+      int issued = 0;
+      for (int i = 0; i < nchunks; ++i) {
+        const int st = i % kStages;
+        if (i >= kStages && !wait_bar_flag(&bar[corr::B_EMPTY + st], ((i - kStages) / kStages) & 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&bar[corr::B_FULL + st], corr::kStageBytes);
+        const int z = (int)(t0 + (int64_t)i * kC);
+        unsigned char* b = base + corr::kSmStage + st * corr::kStageBytes;
+        tc::tma_load_3d(b, &mapPhi, 0, h, z, &bar[corr::B_FULL + st]);
+        tc::tma_load_3d(b + 8192, &mapPhi, 64, h, z, &bar[corr::B_FULL + st]);
+        tc::tma_load_3d(b + corr::kOOff, &mapO, 0, h, z, &bar[corr::B_FULL + st]);
+        issued = i + 1;
+      }
+      if (issued > 0) {
+        const int i = issued - 1;
+        wait_bar_flag(&bar[corr::B_FULL + i % kStages], (i / kStages) & 1, abort_flag);
+      }
+    }
+  } else if (warp == 5) {
+    // ---- MMA: D[buf] = S_in_hi Phi^T + S_in_lo Phi^T (K = 128 in 8 steps of 16 each) ----
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16(128, 64, false, false);
+      bool ok = wait_bar_flag(&bar[corr::B_AREADY], 0, abort_flag);
+      for (int i = 0; ok && i < nchunks; ++i) {
+        const int st = i % kStages, db = i % kDBufs;
+        if (!wait_bar_flag(&bar[corr::B_FULL + st], (i / kStages) & 1, abort_flag)) break;
+        // TMEM buffer db was last read by the epilogue of chunk i - kDBufs
+        if (i >= kDBufs && !wait_bar_flag(&bar[corr::B_TFREE + db], ((i - kDBufs) / kDBufs) & 1, abort_flag)) break;
+        tc::fence_after_sync();
+        const uint64_t dB = tc::kmajor_desc(smem_u32(base + corr::kSmStage + st * corr::kStageBytes), 0, 0);
+        const uint32_t d = tmem + corr::kTmD + (uint32_t)db * 64;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_bf16_ta(d, tmem + corr::kTmAhi + 8 * ks, dB + tc::kmajor_step(8192, ks), idesc, ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          tc::mma_bf16_ta(d, tmem + corr::kTmAlo + 8 * ks, dB + tc::kmajor_step(8192, ks), idesc, true);
+        tc::mma_commit(&bar[corr::B_MMA + db]);
+      }
+      tc::mma_commit(&bar[corr::B_DRAIN]);
+      wait_bar_flag(&bar[corr::B_DRAIN], 0, abort_flag);
+    }
+  } else {
+    const uint32_t lane_base = (uint32_t)(warp * 32);
+    // ---- S_in(seg) as bf16 hi / lo pairs in TMEM (A operand): thread v writes state row v ----
+    {
+      const float* src = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, seg - 1, h) + (size_t)tid * kHeadDim;
+#pragma unroll 1
+      for (int c16 = 0; c16 < 8; ++c16) {
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 x = ld_nc_f4(src + c16 * 16 + 4 * q);
+          split2(x.x, x.y, hi[2 * q], lo[2 * q]);
+          split2(x.z, x.w, hi[2 * q + 1], lo[2 * q + 1]);
+        }
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, corr::kTmAhi + c16 * 8), hi);
+        tc::tmem_st8u(tc::tmem_addr(tmem, lane_base, corr::kTmAlo + c16 * 8), lo);
+      }
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[corr::B_AREADY]);  // one arrival per warp
+    }
+    // ---- epilogue: out tile += D^T, stored back (thread = state row v = tid) ----
+    for (int i = 0; i < nchunks; ++i) {
+      const int st = i % kStages, db = i % kDBufs;
+      int ok = 1;
+      if (tid == 0)
+        ok = (wait_bar_flag(&bar[corr::B_FULL + st], (i / kStages) & 1, abort_flag) &&
+              wait_bar_flag(&bar[corr::B_MMA + db], (i / kDBufs) & 1, abort_flag))
+                 ? 1
+                 : 0;
+      int all;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+          : "=r"(all)
+          : "r"(ok)
+          : "memory");
+      if (!all) break;
+      tc::fence_after_sync();
+      __nv_bfloat16* ot = reinterpret_cast<__nv_bfloat16*>(base + corr::kSmStage + st * corr::kStageBytes + corr::kOOff);
+      float x[64];
+      tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, corr::kTmD + (uint32_t)db * 64), *reinterpret_cast<float(*)[32]>(x));
+      tc::tmem_ld32(tc::tmem_addr(tmem, lane_base, corr::kTmD + (uint32_t)db * 64 + 32),
+                    *reinterpret_cast<float(*)[32]>(x + 32));
+      tc::tmem_wait_ld();
+      tc::fence_before_sync();
+      named_sync(1, 128);
+      if (tid == 0) mbar_arrive(&bar[corr::B_TFREE + db]);  // D buffer read: the next MMA may overwrite it
+#pragma unroll
+      for (int u = 0; u < 64; ++u) {
+        __nv_bfloat16* e = ot + u * kHeadDim + tid;
+        *e = __float2bfloat16_rn(__bfloat162float(*e) + x[u]);
+      }
+      tc::fence_proxy_async_smem();  // the tile is read by the TMA store
+      named_sync(1, 128);
+      if (tid == 0) {
+        const int64_t rem = len - (int64_t)i * kC;
+        const int nvalid = rem < kC ? (int)rem : kC;
+        const int64_t z = t0 + (int64_t)i * kC;
+        if (nvalid == kC) {
+          tc::tma_store_3d(&mapO, 0, h, (int)z, ot);
+        } else {  // the sequence's last, partial chunk: only its own rows
+          __nv_bfloat16* out = p.out + z * p.o_st + (int64_t)h * p.o_sh;
+          for (int t = 0; t < nvalid; ++t) tc::bulk_s2g(out + (int64_t)t * p.o_st, ot + t * kHeadDim, 256);
+        }
+        tc::bulk_commit();
+        // the previous chunk's store has read its tile (this one's may still be reading):
+        // that stage may be refilled
+        if (i >= 1) {
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          mbar_arrive(&bar[corr::B_EMPTY + (i - 1) % kStages]);
+        }
+      }
+    }
+    if (tid == 0) tc::bulk_wait_all();
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 5) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, corr::kTmemCols);
   }
 }
 
@@ -926,33 +1163,104 @@ __global__ void __launch_bounds__(256) map_combine_kernel(PrefillParams p) {
 }  // namespace
 
 cudaError_t launch_prefill_combine(const PrefillParams& p, cudaStream_t stream) {
-  if (p.cp_segments < 3) return cudaSuccess;
+  if (p.cp_segments < 2) return cudaSuccess;
   prefill_combine_kernel<<<dim3(p.HV, p.N, kHeadDim / 32), 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
-int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
-  const int req = (int)((flags >> kPrefillSegmentsShift) & 15u);
-  if (req >= 1) return req;
-  // automatic, for sequences of 16 chunks or more on average.  With c (sequence, v-head)
-  // chains and m SMs, one chain per sequence takes waves(c) = ceil(c / m) chain-lengths;
-  // S segments take waves(c (2 S - 3)) + waves(c (S - 1)) segment-lengths of 1/S (pass 1
-  // and the reruns).  The cheapest S in [3, 8] is used if it saves at least 10 %.
-  const int64_t chains = (int64_t)num_seqs * num_v_heads;
-  if (chains <= 0 || total_tokens < (int64_t)num_seqs * 16 * kC) return 1;
-  const int64_t sms = device_sm_count();
-  auto waves = [&](int64_t ctas) { return (double)((ctas + sms - 1) / sms); };
-  const double one = waves(chains);
-  double best = one;
-  int best_s = 1;
-  for (int sg = 3; sg <= 8; ++sg) {
-    const double cost = (waves(chains * (2 * sg - 3)) + waves(chains * (sg - 1))) / sg;
-    if (cost < best) {
-      best = cost;
-      best_s = sg;
+namespace {
+// How the chunked prefill cuts sequences into context-parallel segments.
+struct CpPlan {
+  int S = 1;      // segments per sequence (1: none)
+  int w0 = 1024;  // segment 0's share of a sequence's chunks, in 1/1024
+};
+
+// Makespan, in chain-lengths, of longest-first list scheduling of `na` jobs of length a and
+// `nb` jobs of length b on m SMs (CTAs start in blockIdx order as SMs free up).
+double lpt_makespan(int64_t na, double a, int64_t nb, double b, int64_t m) {
+  std::priority_queue<double, std::vector<double>, std::greater<double>> load;
+  for (int64_t i = 0; i < m; ++i) load.push(0.0);
+  auto place = [&](int64_t cnt, double len) {
+    for (int64_t i = 0; i < cnt; ++i) {
+      const double x = load.top();
+      load.pop();
+      load.push(x + len);
     }
+  };
+  if (a >= b) {
+    place(na, a);
+    place(nb, b);
+  } else {
+    place(nb, b);
+    place(na, a);
   }
-  return best <= 0.9 * one ? best_s : 1;
+  double mk = 0.0;
+  while (!load.empty()) {
+    mk = load.top() > mk ? load.top() : mk;
+    load.pop();
+  }
+  return mk;
+}
+
+// Automatic plan for c (sequence, v-head) chains of about 2^lg_chunks chunks on m SMs.
+// Without segments the chains take waves(c) = ceil(c / m) chain-lengths.  With S segments,
+// segment 0 (fraction a of the chunks) is one chain with outputs and every later segment
+// two (its maps, with the homogeneous outputs), so pass 1 is c jobs of length a and
+// 2 c (S - 1) jobs of length (1 - a) / (S - 1), each plus a fixed ~2 chunks (CTA start,
+// pipeline fill), then the output correction (one memory-bound pass over the later
+// segments' tokens, ~0.0035 c (1 - a) chain-lengths, measured) and the map composition
+// (~0.01).
+// Candidates: S in [2, 8], segment 0 1 .. 4 times as long as the others; used if it saves
+// at least 10 %.
+CpPlan cp_plan_auto(int64_t chains, int64_t sms, int lg_chunks) {
+  static std::mutex mu;
+  static std::map<std::pair<int64_t, int64_t>, CpPlan> cache;
+  const std::pair<int64_t, int64_t> key(chains * 64 + lg_chunks, sms);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  CpPlan plan;
+  const double one = (double)((chains + sms - 1) / sms);
+  if (chains < 4 * sms) {
+    double best = one;
+    const double eps = 2.0 / (double)(1LL << lg_chunks);
+    const double ks[] = {1.0, 1.5, 2.0, 2.5, 3.0, 4.0};
+    for (int sg = 2; sg <= 8; ++sg) {
+      for (double k : ks) {
+        const double a = k / (k + sg - 1);
+        const double cost =
+            lpt_makespan(chains, a + eps, 2 * chains * (sg - 1), (1.0 - a) / (sg - 1) + eps, sms) +
+            0.0035 * (double)chains * (1.0 - a) + 0.01;
+        if (cost < best - 1e-9) {
+          best = cost;
+          plan.S = sg;
+          plan.w0 = (int)(a * 1024.0 + 0.5);
+        }
+      }
+    }
+    if (best > 0.9 * one) plan = CpPlan();
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = plan;
+  return plan;
+}
+
+CpPlan cp_plan(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  const int req = (int)((flags >> kPrefillSegmentsShift) & 15u);
+  if (req >= 1) return CpPlan{req, req > 1 ? 1024 / req : 1024};  // forced: equal segments
+  // automatic, for sequences of 16 chunks or more on average
+  const int64_t chains = (int64_t)num_seqs * num_v_heads;
+  if (chains <= 0 || total_tokens < (int64_t)num_seqs * 16 * kC) return CpPlan();
+  int lg = 4;  // floor(log2(average chunks per sequence)), 16 .. 2^20
+  while (lg < 20 && total_tokens >= (int64_t)num_seqs * kC * (2LL << lg)) ++lg;
+  return cp_plan_auto(chains, device_sm_count(), lg);
+}
+}  // namespace
+
+int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  return cp_plan(num_seqs, total_tokens, num_v_heads, flags).S;
 }
 
 int prefill_map_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
@@ -988,13 +1296,23 @@ size_t prefill_map_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v
 }
 
 namespace {
-// Workspace of the chunked prefill: [records][context-parallel scratch (segments)][q norms
-// (GDN_FLAG_QK_L2NORM: [T][HQ] float2, sized for HV >= HQ heads)], each part 256-byte aligned.
+// Workspace of the chunked prefill: [records][context-parallel states and maps][Phi (the
+// segments' homogeneous outputs, [T][HV][128] bf16)][q norms (GDN_FLAG_QK_L2NORM: [T][HQ]
+// float2, sized for HV >= HQ heads)], each part 256-byte aligned; no segment parts without
+// segments.
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+size_t chunk_records_bytes(int num_seqs, int64_t total_tokens, int num_v_heads) {
+  return (size_t)chunk::num_slots(total_tokens, num_seqs) * (size_t)num_v_heads * chunk::kRecBytes;
+}
+size_t cp_states_bytes(int num_seqs, int num_v_heads, int S) {
+  return (size_t)cp_floats(num_seqs, num_v_heads, S) * sizeof(float);
+}
 size_t chunk_records_and_cp_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
-  const size_t records = (size_t)chunk::num_slots(total_tokens, num_seqs) * (size_t)num_v_heads * chunk::kRecBytes;
+  const size_t records = chunk_records_bytes(num_seqs, total_tokens, num_v_heads);
   const int S = prefill_cp_segments(num_seqs, total_tokens, num_v_heads, flags);
   if (S <= 1) return records;
-  return ((records + 255) & ~(size_t)255) + (size_t)cp_floats(num_seqs, num_v_heads, S) * sizeof(float);
+  return align256(records) + align256(cp_states_bytes(num_seqs, num_v_heads, S)) +
+         (size_t)total_tokens * (size_t)num_v_heads * kHeadDim * sizeof(__nv_bfloat16);
 }
 }  // namespace
 
@@ -1085,7 +1403,7 @@ cudaError_t launch_prefill_state_map(const PrefillParams& p, cudaStream_t stream
   CUtensorMap mk, mq, mv, mo;
   cudaError_t e = prefill_setup(q, stream, &mk, &mq, &mv, &mo);
   if (e != cudaSuccess) return e;
-  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2 * S), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2 * S), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, mo, q);
   e = cudaGetLastError();
   if (e != cudaSuccess || S == 1) return e;
   map_combine_kernel<<<dim3(p.HV, p.N, 8), 256, 0, stream>>>(q);
@@ -1097,32 +1415,56 @@ cudaError_t launch_prefill_chunk(const PrefillParams& p_in, cudaStream_t stream)
   PrefillParams p = p_in;
   if (p.flags & kFlagQkL2Norm) {
     const size_t base = chunk_records_and_cp_bytes(p.N, p.T, p.HV, p.flags);
-    p.qnorm = reinterpret_cast<float2*>(static_cast<unsigned char*>(p.workspace) + ((base + 255) & ~(size_t)255));
+    p.qnorm = reinterpret_cast<float2*>(static_cast<unsigned char*>(p.workspace) + align256(base));
   }
   CUtensorMap mk, mq, mv, mo;
   cudaError_t e = prefill_setup(p, stream, &mk, &mq, &mv, &mo);
   if (e != cudaSuccess) return e;
-  const int S = prefill_cp_segments(p.N, p.T, p.HV, p.flags);
-  if (S <= 1) {
+  const CpPlan plan = cp_plan(p.N, p.T, p.HV, p.flags);
+  if (plan.S <= 1) {
     PrefillParams q = p;
     q.cp_segments = 1;
     q.cp_pass = 0;
-    prefill_chunk_kernel<<<dim3(p.HV, p.N), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+    prefill_chunk_kernel<<<dim3(p.HV, p.N), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, mo, q);
     return cudaGetLastError();
   }
-  // context parallelism: segment maps, their composition, the segment reruns
-  const size_t records = (size_t)chunk::num_slots(p.T, p.N) * (size_t)p.HV * chunk::kRecBytes;
+  // context parallelism: segment 0 and the later segments' maps with their homogeneous
+  // outputs (one launch), the map composition (initial states, final state), the output
+  // correction of the later segments
+  const int S = plan.S;
+  unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+  const size_t states_at = align256(chunk_records_bytes(p.N, p.T, p.HV));
   PrefillParams q = p;
   q.cp_segments = S;
-  q.cp_scratch = reinterpret_cast<float*>(static_cast<unsigned char*>(p.workspace) + ((records + 255) & ~(size_t)255));
+  q.cp_w0 = plan.w0;
   q.cp_pass = 1;
-  prefill_chunk_kernel<<<dim3(p.HV, p.N, S >= 3 ? 2 * S - 3 : 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  q.cp_scratch = reinterpret_cast<float*>(ws + states_at);
+  q.cp_phi = reinterpret_cast<__nv_bfloat16*>(ws + states_at + align256(cp_states_bytes(p.N, p.HV, S)));
+  CUtensorMap mphi_st, mphi_ld;
+  const int64_t phi_st = (int64_t)p.HV * kHeadDim;
+  if (!make_map(&mphi_st, q.cp_phi, p.T, p.HV, phi_st, kHeadDim, 128, false) ||
+      !make_map(&mphi_ld, q.cp_phi, p.T, p.HV, phi_st, kHeadDim, 64, true))
+    return cudaErrorInvalidValue;
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2 * S - 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, mphi_st, q);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   e = launch_prefill_combine(q, stream);
   if (e != cudaSuccess) return e;
-  q.cp_pass = 3;
-  prefill_chunk_kernel<<<dim3(p.HV, p.N, S - 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo, q);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(prefill_correct_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)corr::kSmAlloc);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  // each CTA corrects ~16 chunks of one segment
+  const int64_t seg_chunks = (p.T / p.N / kC) * (1024 - plan.w0) / 1024 / (S - 1);
+  q.cp_parts = (int)(seg_chunks / 16 < 1 ? 1 : (seg_chunks / 16 > 64 ? 64 : seg_chunks / 16));
+  prefill_correct_kernel<<<dim3(p.HV, p.N, (S - 1) * q.cp_parts), corr::kThreads, corr::kSmAlloc, stream>>>(
+      mphi_ld, mo, q);
   return cudaGetLastError();
 }
 

@@ -75,21 +75,35 @@ __host__ __device__ inline int64_t num_slots(int64_t total_tokens, int num_seqs)
   return total_tokens / kC + num_seqs + 1;
 }
 
-// Context-parallel scratch: three arrays of [N][count][HV][128 x 128] fp32 states
-//   kCpIn  count S - 1: the initial state of segment idx + 1
-//   kCpMap count S - 2: M of segment idx + 1 (its state map is S_out = S_in M + C)
-//   kCpOff count S - 2: C of segment idx + 1
+// Context-parallel scratch (a sequence's chunks cut into S >= 2 segments): three arrays of
+// [N][S - 1][HV][128 x 128] fp32 states, idx = segment - 1:
+//   kCpIn  the initial state of segment idx + 1
+//   kCpMap M of segment idx + 1 (its state map is S_out = S_in M + C)
+//   kCpOff C of segment idx + 1
+// followed (256-byte aligned) by Phi [T][HV][128] bf16: the outputs of each segment's
+// homogeneous chain (run from the identity with v = 0), for the output correction.
 enum CpArray { kCpIn = 0, kCpMap = 1, kCpOff = 2 };
 constexpr int64_t kStateFloats = 128 * 128;
 __host__ __device__ inline int64_t cp_floats(int N, int HV, int S) {
-  return S < 3 ? (S == 2 ? (int64_t)N * HV * kStateFloats : 0) : (int64_t)N * HV * kStateFloats * (3 * S - 5);
+  return S < 2 ? 0 : (int64_t)N * HV * kStateFloats * 3 * (S - 1);
 }
 __host__ __device__ inline int64_t cp_offset(int N, int HV, int S, int which, int n, int idx, int h) {
-  const int64_t in_n = (int64_t)N * (S - 1) * HV * kStateFloats;
-  const int64_t map_n = S >= 3 ? (int64_t)N * (S - 2) * HV * kStateFloats : 0;
-  const int count = which == kCpIn ? S - 1 : S - 2;
-  const int64_t base = which == kCpIn ? 0 : (which == kCpMap ? in_n : in_n + map_n);
-  return base + (((int64_t)n * count + idx) * HV + h) * kStateFloats;
+  const int64_t per_array = (int64_t)N * (S - 1) * HV * kStateFloats;
+  return which * per_array + (((int64_t)n * (S - 1) + idx) * HV + h) * kStateFloats;
+}
+// Chunk range [cb, ce) of segment `seg` of a sequence of `nch` chunks cut into S segments:
+// segment 0 (one chain, with outputs) takes w0 / 1024 of the chunks, the others (two chains
+// each: the maps) share the rest evenly.
+__host__ __device__ inline void segment_range(int nch, int S, int w0, int seg, int& cb, int& ce) {
+  const int c0 = S <= 1 ? nch : (int)(((int64_t)nch * w0) >> 10);
+  if (seg == 0) {
+    cb = 0;
+    ce = c0;
+    return;
+  }
+  const int rest = nch - c0;
+  cb = c0 + (int)((int64_t)(seg - 1) * rest / (S - 1));
+  ce = c0 + (int)((int64_t)seg * rest / (S - 1));
 }
 
 // State-map scratch when the map of each sequence is computed in S segments:

@@ -107,19 +107,24 @@ def test_workspace_size(lib):
 
 
 def test_workspace_size_with_segments(lib):
-    """Context-parallel segments add [N][3 S - 5][HV] 64 KB states (segment starts,
-    maps M and C) after the records, 256-byte aligned.  Automatic: one long sequence
-    with 32 v-heads (32 chains on 148 SMs) gets S = 5 (pass 1: 224 CTAs in 2 waves,
-    reruns: 128 in 1 wave, 3/5 of one chain's length); many or short sequences get none."""
+    """Context-parallel segments (S per sequence) add, after the records (256-byte aligned):
+    [3][N][S - 1][HV] 64 KB states (the later segments' initial states, maps M and C), then
+    Phi, the later segments' homogeneous outputs, [T][HV][128] bf16.  Automatic (no GPU here:
+    148 SMs assumed): a plan is used when it beats one chain per (sequence, v-head) by 10 %;
+    one 4096-token sequence with 32 v-heads (32 chains) gets 4 segments, two 8192-token
+    sequences (64 chains) get 2 (segment 0 two thirds of the chunks, its chain beside the
+    two map chains of the rest), many or short sequences none."""
     seg = lambda n: (n & 15) << 8  # noqa: E731  (GDN_PREFILL_SEGMENTS)
     rec = lambda n, t: (t // 64 + n + 1) * 32 * 11008  # noqa: E731
+    phi = lambda t: t * 32 * 128 * 2  # noqa: E731
     st = 128 * 128 * 4
-    assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(3)) == rec(2, 3000) + 2 * 32 * st * 4
-    assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(2)) == rec(2, 3000) + 2 * 32 * st * 1
+    assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(3)) == rec(2, 3000) + 3 * 2 * 2 * 32 * st + phi(3000)
+    assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(2)) == rec(2, 3000) + 3 * 2 * 1 * 32 * st + phi(3000)
     assert lib.gdn_prefill_workspace_size(2, 3000, 16, 32, 128, seg(1)) == rec(2, 3000)
-    assert lib.gdn_prefill_workspace_size(1, 4096, 16, 32, 128, 0) == rec(1, 4096) + 32 * st * 10
+    assert lib.gdn_prefill_workspace_size(1, 4096, 16, 32, 128, 0) == rec(1, 4096) + 3 * 3 * 32 * st + phi(4096)
+    assert lib.gdn_prefill_workspace_size(2, 8192, 16, 32, 128, 0) == rec(2, 8192) + 3 * 2 * 32 * st + phi(8192)
     assert lib.gdn_prefill_workspace_size(1, 512, 16, 32, 128, 0) == rec(1, 512)  # < 16 chunks
-    assert lib.gdn_prefill_workspace_size(2, 8192, 16, 32, 128, 0) == rec(2, 8192)  # 64 chains
+    assert lib.gdn_prefill_workspace_size(4, 4 * 8192, 16, 32, 128, 0) == rec(4, 4 * 8192)  # 128 chains
     # gdn_prefill_state_map (GDN_FLAG_STATE_MAP): records + [2][N][S][HV] segment maps; one long
     # 32-head sequence gets S = 2 (128 chains, one wave, half the chunks each)
     smap = 0x4

@@ -32,12 +32,12 @@ def test_noalloc_rejects_problems_beyond_the_scratch(gdn):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("lens, segments", [([100, 64, 0, 257, 1, 700], 0), ([1500, 0, 700], 3)])
+@pytest.mark.parametrize("lens, segments", [([100, 64, 0, 257, 1, 700], 0), ([1500, 0, 700], 2)])
 def test_noalloc_twice_matches_workspace_entry_point(gdn, lens, segments):
     """Two no-alloc calls in a row give the same outputs and states, bit for bit, as
     ``gdn_prefill`` with a caller workspace (same kernels, same inputs).  The second case
-    forces 3 context-parallel segments, so the static scratch also holds segment states
-    and maps (after the records) that the calls must fully rewrite."""
+    forces 2 context-parallel segments, so the static scratch also holds segment states,
+    maps and homogeneous outputs (after the records) that the calls must fully rewrite."""
     inp = to_dev(gdn.workloads.prefill_inputs(lens, seed=77))
     T, HV = inp["v"].shape[0], inp["v"].shape[1]
     N = inp["cu_seqlens"].shape[0] - 1
