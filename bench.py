@@ -770,7 +770,8 @@ def run_ours(args, world, rank, local):
                           config={"workload": wl, "batch_per_rank": mb, "tokens_per_seq": mt,
                                   "pool_slots": 3 * mb, "l2": "3 disjoint slot sets, 805 MB pool",
                                   "parallelism": f"dp{world}"},
-                          roofline=mres["roofline"], gpu_launches=msteps, clocks=mres["clocks"], e2e=None)
+                          roofline=mres["roofline"], gpu_launches=msteps, clocks=mres["clocks"], e2e=None,
+                          tokens_sweep=sweep)
         else:
             result["mtp"] = mres
         del msets
