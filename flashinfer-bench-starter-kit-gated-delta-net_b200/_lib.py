@@ -21,6 +21,7 @@ GDN_ERR_WORKSPACE = 4
 GDN_FLAG_QK_L2NORM = 0x1
 GDN_FLAG_PREFILL_SERIAL = 0x2
 GDN_FLAG_STATE_MAP = 0x4
+GDN_FLAG_RANGE_AFFINE = 0x8
 GDN_FLAG_SELFTEST_WAIT_TIMEOUT = 0x80000000
 
 
@@ -78,6 +79,19 @@ SIGNATURES = {
                                _P, _I64, _I64, _P, _I64, _I64,                   # map_m, map_c
                                _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
                                _P, _SZ, _U32, _P], ctypes.c_int),
+    "gdn_prefill_range_affine": ([_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,  # q, k, v
+                                  _P, _P, _I64, _P, _P, _I64,                       # A_log, a, dt_bias, b
+                                  _P, _I32, _F,                                     # cu_seqlens, scale
+                                  _P, _I64, _I64,                                   # out
+                                  _P, _I64, _I64, _P, _I64, _I64,                   # map_m, map_c
+                                  _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
+                                  _P, _SZ, _U32, _P], ctypes.c_int),
+    "gdn_prefill_range_finish": ([_P, _I32,                                         # cu_seqlens
+                                  _P, _I64, _I64,                                   # state (S_in)
+                                  _P, _I64, _I64,                                   # out
+                                  _P, _I64, _I64,                                   # new_state
+                                  _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D
+                                  _P, _SZ, _U32, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -3,34 +3,31 @@ of a process group, each rank holding a contiguous token range of every sequence
 
 The GDN recurrence is affine in the state: running a token range from initial state
 S gives ``S_out = S @ M + C`` per (sequence, v-head), with M [K x K] the range run
-from the identity with v taken as 0 and C [V x K] the range run from zero
-(``kernel_prefill.state_map``, C ABI ``gdn_prefill_state_map``).  So:
+from the identity with v taken as 0 and C [V x K] the range run from zero, and the
+range's outputs are affine in S too (``o_t = o_t(0) + S @ Phi_t``, Phi the outputs of
+the run from the identity).  So:
 
 1. rank 0 runs its ranges from the sequences' initial state (outputs and the state
-   leaving its ranges); every other rank meanwhile computes its ranges' maps;
+   leaving its ranges); every other rank meanwhile runs ``kernel_prefill.range_affine``
+   on its ranges: their outputs from a zero state, their maps, and (kept on the GPU)
+   the homogeneous outputs;
 2. one ``all_gather`` of ``[2, N, HV, 128, 128]`` fp32 per rank: rank 0 sends
    ``(0, S_end)``, rank r sends ``(M_r, C_r)`` (the one exchange step of d x d
    matrices per range);
 3. rank r > 0 folds ``S <- S @ M_j + C_j`` over j < r from ``S = 0`` (rank 0's pair
-   gives ``S_end``) to get the state entering its ranges, and reruns them with outputs;
+   gives ``S_end``) to get the state entering its ranges, and ``range_finish`` adds that
+   state's share to its outputs and gives the state leaving them (no token runs twice);
 4. the last rank's final state is broadcast, so every rank returns the sequences'
    final state.
 
-Each rank but rank 0 works two range-lengths (the map, itself computed in segments
-on separate SMs, then the rerun), rank 0 one; both use the in-GPU segment split of
-``kernel_prefill`` for few long sequences.  The
-reference has no long-context parallelism (its prefill is token-serial per
-sequence, ``solution/triton/kernel_prefill.py:88``).
+Both rank 0's prefill and the other ranks' affine pass cut their ranges into segments on
+separate SMs (one long 32-head sequence: rank 0's prefill ~0.45 and an affine pass ~0.5 of
+one chain per token, the finish ~0.1 more after the exchange), so rank 0's range is
+weighted ``FIRST_RANK_WEIGHT`` = 1.2 times the others'.  The reference has no long-context
+parallelism (its prefill is token-serial per sequence, ``solution/triton/kernel_prefill.py:88``).
 
 ``split_ranges``/``local_inputs`` cut a global varlen batch into rank-local inputs:
-every range of a sequence starts on a 64-token chunk boundary.  The reruns need the
-state leaving rank 0's range, so rank 0's prefill and the other ranks' maps form the
-first stage of the critical path and the reruns the second: rank 0's range is weighted
-``FIRST_RANK_WEIGHT`` times the others' so that its prefill ends with their maps (with
-the in-GPU segments of one long 32-head sequence a map costs ~0.5 and a prefill ~0.6
-of one chain per token: 0.5 / 0.6 ≈ 0.8).  A step then takes ~1.1 range-lengths of one
-chain on each rank against ~0.6 sequence-lengths on one GPU: about even at 2 ranks,
-~2x at 4, ~4x at 8.
+every range of a sequence starts on a 64-token chunk boundary.
 """
 from __future__ import annotations
 
@@ -41,7 +38,7 @@ import torch
 import torch.distributed as dist
 
 CHUNK = 64
-FIRST_RANK_WEIGHT = 0.8
+FIRST_RANK_WEIGHT = 1.2
 
 
 def split_ranges(seqlens, world: int, first_weight: float = FIRST_RANK_WEIGHT) -> list[list[tuple[int, int]]]:
@@ -90,7 +87,8 @@ class Ops:
     """The per-rank computations (the CUDA kernels by default; tests substitute a CPU
     implementation to exercise the exchange on gloo ranks)."""
     prefill: Callable  # (q,k,v,state,A_log,a,dt_bias,b,cu_seqlens,scale) -> (out, final_state)
-    state_map: Callable  # (q,k,v,A_log,a,dt_bias,b,cu_seqlens) -> (M, C)
+    affine: Callable  # (q,k,v,A_log,a,dt_bias,b,cu_seqlens,scale) -> (handle, M, C)
+    finish: Callable  # (handle, S_in) -> (out, final_state)
     compose: Callable  # (S, M, C) -> S @ M + C   (per sequence and v-head, fp32)
 
 
@@ -100,7 +98,11 @@ def cuda_ops() -> Ops:
     def compose(S, M, C):
         return torch.baddbmm(C.flatten(0, 1), S.flatten(0, 1), M.flatten(0, 1)).view_as(C)
 
-    return Ops(prefill=kernel_prefill.run, state_map=kernel_prefill.state_map, compose=compose)
+    def affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale):
+        h = kernel_prefill.range_affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale)
+        return h, h.map_m, h.map_c
+
+    return Ops(prefill=kernel_prefill.run, affine=affine, finish=kernel_prefill.range_finish, compose=compose)
 
 
 def prefill_context_parallel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, group=None,
@@ -120,7 +122,7 @@ def prefill_context_parallel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, s
         out, s_end = ops.prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
         pair = torch.stack([torch.zeros_like(s_end), s_end])
     else:
-        m, c = ops.state_map(q, k, v, A_log, a, dt_bias, b, cu_seqlens)
+        handle, m, c = ops.affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale)
         pair = torch.stack([m, c])
     pairs = [torch.empty(2, N, HV, D, D, dtype=torch.float32, device=dev) for _ in range(world)]
     dist.all_gather(pairs, pair.contiguous(), group=group)
@@ -128,7 +130,7 @@ def prefill_context_parallel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, s
         s_in = torch.zeros(N, HV, D, D, dtype=torch.float32, device=dev)
         for j in range(rank):
             s_in = ops.compose(s_in, pairs[j][0], pairs[j][1])
-        out, s_end = ops.prefill(q, k, v, s_in, A_log, a, dt_bias, b, cu_seqlens, scale)
+        out, s_end = ops.finish(handle, s_in)
     final = s_end.contiguous() if rank == world - 1 else torch.empty(N, HV, D, D, dtype=torch.float32, device=dev)
     src = dist.get_global_rank(group, world - 1) if group is not None else world - 1
     dist.broadcast(final, src=src, group=group)

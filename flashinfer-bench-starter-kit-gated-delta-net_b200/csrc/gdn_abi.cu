@@ -177,6 +177,9 @@ size_t gdn_prefill_workspace_size(int32_t num_seqs, int64_t total_tokens, int32_
                                   int32_t head_dim, uint32_t flags) {
   (void)num_qk_heads;
   (void)head_dim;
+  // gdn_prefill_range_affine / _finish: records, segment states and maps, homogeneous outputs
+  if (flags & GDN_FLAG_RANGE_AFFINE)
+    return gdn::prefill_range_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
   // gdn_prefill_state_map: records + the per-segment maps
   if (flags & GDN_FLAG_STATE_MAP) return gdn::prefill_map_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
   // the token-serial kernel (forced) needs none; the chunked kernel keeps one prepared
@@ -420,6 +423,140 @@ int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_stride_h,
   const cudaError_t e = total_tokens > 0 ? gdn::launch_prefill_state_map(p, static_cast<cudaStream_t>(stream))
                                          : gdn::launch_identity_maps(p, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill_state_map launch");
+  return ok();
+}
+
+int gdn_prefill_range_affine(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+                             int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_t,
+                             int64_t v_stride_h, const float* A_log, const void* a, int64_t a_stride_t,
+                             const float* dt_bias, const void* b, int64_t b_stride_t, const void* cu_seqlens,
+                             int32_t cu_seqlens_is_int64, float scale, void* out, int64_t out_stride_t,
+                             int64_t out_stride_h, float* map_m, int64_t map_m_stride_n, int64_t map_m_stride_h,
+                             float* map_c, int64_t map_c_stride_n, int64_t map_c_stride_h, int32_t num_seqs,
+                             int64_t total_tokens, int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                             void* workspace, size_t workspace_bytes, uint32_t flags, void* stream) {
+  int rc = check_common(num_qk_heads, num_v_heads, head_dim);
+  if (rc) return rc;
+  if (num_seqs < 0 || total_tokens < 0)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0 (got %d, %lld)", num_seqs,
+                (long long)total_tokens);
+  if (num_seqs > 65535) return fail(GDN_ERR_UNSUPPORTED, "num_seqs > 65535 per call is not supported");
+  if (flags & ~(GDN_FLAG_RANGE_AFFINE | GDN_PREFILL_SEGMENTS(15)))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_prefill_range_affine: unsupported flag bits 0x%x", flags);
+  if (num_seqs == 0) return ok();
+  if (!cu_seqlens || !A_log || !dt_bias || !map_m || !map_c)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (!aligned(map_m, map_m_stride_n, map_m_stride_h, sizeof(float), 16) ||
+      !aligned(map_c, map_c_stride_n, map_c_stride_h, sizeof(float), 16))
+    return fail(GDN_ERR_UNSUPPORTED, "map rows must be 16-byte aligned (base and strides)");
+  if (total_tokens > 0) {
+    if (!q || !k || !v || !a || !b || !out) return fail(GDN_ERR_INVALID_ARGUMENT, "a required tensor pointer is NULL");
+    if (!aligned(q, q_stride_t, q_stride_h, 2, 16) || !aligned(k, k_stride_t, k_stride_h, 2, 16) ||
+        !aligned(v, v_stride_t, v_stride_h, 2, 16))
+      return fail(GDN_ERR_UNSUPPORTED, "gdn_prefill_range_affine needs 16-byte aligned q/k/v rows (base and strides)");
+    if ((reinterpret_cast<uintptr_t>(out) & 15) || (out_stride_t & 7) || (out_stride_h & 7))
+      return fail(GDN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned (base and strides)");
+  }
+  const size_t need = gdn::prefill_range_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required (got %zu)", need,
+                workspace_bytes);
+  gdn::PrefillParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.state = nullptr;
+  p.A_log = A_log;
+  p.a = static_cast<const __nv_bfloat16*>(a);
+  p.dt_bias = dt_bias;
+  p.b = static_cast<const __nv_bfloat16*>(b);
+  p.cu_seqlens = cu_seqlens;
+  p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.new_state = nullptr;
+  p.q_st = q_stride_t;
+  p.q_sh = q_stride_h;
+  p.k_st = k_stride_t;
+  p.k_sh = k_stride_h;
+  p.v_st = v_stride_t;
+  p.v_sh = v_stride_h;
+  p.s_sn = p.s_sh = 0;
+  p.a_st = a_stride_t;
+  p.b_st = b_stride_t;
+  p.o_st = out_stride_t;
+  p.o_sh = out_stride_h;
+  p.n_sn = p.n_sh = 0;
+  p.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim);
+  p.N = num_seqs;
+  p.HQ = num_qk_heads;
+  p.HV = num_v_heads;
+  p.ratio = num_v_heads / num_qk_heads;
+  p.T = total_tokens;
+  p.flags = flags;
+  p.workspace = workspace;
+  p.workspace_bytes = workspace_bytes;
+  p.map_m = map_m;
+  p.m_sn = map_m_stride_n;
+  p.m_sh = map_m_stride_h;
+  p.map_c = map_c;
+  p.c_sn = map_c_stride_n;
+  p.c_sh = map_c_stride_h;
+  const cudaError_t e = total_tokens > 0 ? gdn::launch_prefill_range_affine(p, static_cast<cudaStream_t>(stream))
+                                         : gdn::launch_identity_maps(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill_range_affine launch");
+  return ok();
+}
+
+int gdn_prefill_range_finish(const void* cu_seqlens, int32_t cu_seqlens_is_int64, const float* state,
+                             int64_t state_stride_n, int64_t state_stride_h, void* out, int64_t out_stride_t,
+                             int64_t out_stride_h, float* new_state, int64_t new_state_stride_n,
+                             int64_t new_state_stride_h, int32_t num_seqs, int64_t total_tokens,
+                             int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim, void* workspace,
+                             size_t workspace_bytes, uint32_t flags, void* stream) {
+  int rc = check_common(num_qk_heads, num_v_heads, head_dim);
+  if (rc) return rc;
+  if (num_seqs < 0 || total_tokens < 0)
+    return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs and total_tokens must be >= 0 (got %d, %lld)", num_seqs,
+                (long long)total_tokens);
+  if (num_seqs > 65535) return fail(GDN_ERR_UNSUPPORTED, "num_seqs > 65535 per call is not supported");
+  if (flags & ~(GDN_FLAG_RANGE_AFFINE | GDN_PREFILL_SEGMENTS(15)))
+    return fail(GDN_ERR_INVALID_ARGUMENT, "gdn_prefill_range_finish: unsupported flag bits 0x%x", flags);
+  if (num_seqs == 0) return ok();
+  if (!cu_seqlens) return fail(GDN_ERR_INVALID_ARGUMENT, "cu_seqlens must not be NULL");
+  if (total_tokens > 0) {
+    if (!out) return fail(GDN_ERR_INVALID_ARGUMENT, "out must not be NULL");
+    if ((reinterpret_cast<uintptr_t>(out) & 15) || (out_stride_t & 7) || (out_stride_h & 7))
+      return fail(GDN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned (base and strides)");
+  }
+  rc = check_state_pair(state, state_stride_n, state_stride_h, new_state, new_state_stride_n, new_state_stride_h,
+                        num_seqs, num_v_heads);
+  if (rc) return rc;
+  const size_t need = gdn::prefill_range_workspace_bytes(num_seqs, total_tokens, num_v_heads, flags);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required (got %zu)", need,
+                workspace_bytes);
+  gdn::PrefillParams p;
+  p.cu_seqlens = cu_seqlens;
+  p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
+  p.state = state;
+  p.s_sn = state_stride_n;
+  p.s_sh = state_stride_h;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_st = out_stride_t;
+  p.o_sh = out_stride_h;
+  p.new_state = new_state;
+  p.n_sn = new_state_stride_n;
+  p.n_sh = new_state_stride_h;
+  p.N = num_seqs;
+  p.HQ = num_qk_heads;
+  p.HV = num_v_heads;
+  p.ratio = num_v_heads / num_qk_heads;
+  p.T = total_tokens;
+  p.flags = flags;
+  p.workspace = workspace;
+  p.workspace_bytes = workspace_bytes;
+  const cudaError_t e = gdn::launch_prefill_range_finish(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill_range_finish launch");
   return ok();
 }
 

@@ -74,6 +74,10 @@ struct PrefillParams {
   int cp_pass = 0;
   int cp_w0 = 0;
   int cp_parts = 1;  // output correction: CTAs per segment (each a contiguous part of its chunks)
+  // map composition: 0 = segment initial states from kCpIn[0] (in-GPU prefill), 3 = from
+  // state (a range's incoming state, also copied to kCpIn[0]), both ending in new_state;
+  // 1 = the range's M (from the identity, no C) into map_m, 2 = its C (from zero) into map_c
+  int cp_combine = 0;
   float* cp_scratch = nullptr;
   __nv_bfloat16* cp_phi = nullptr;
   // GDN_FLAG_QK_L2NORM: per (token, q/k head) (1 / |q|, log2 (1 / |q|)), [T][HQ] (workspace)
@@ -128,6 +132,15 @@ size_t prefill_chunk_workspace_bytes(int num_seqs, int64_t total_tokens, int num
 // flags bits kPrefillSegmentsShift .. + 3 request a count (0 = automatic).
 constexpr int kPrefillSegmentsShift = 8;
 int prefill_cp_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
+// Context parallelism across GPUs, a rank holding a later token range of each sequence: the
+// range as map-pair segments only, with outputs from a zero initial state and the
+// homogeneous outputs (launch_prefill_range_affine: out, map_m, map_c), then, once the state
+// entering the range is known (p.state), the output correction and the final state
+// (launch_prefill_range_finish).  Both take the same workspace (prefill_range_workspace_bytes).
+int prefill_range_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
+size_t prefill_range_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags);
+cudaError_t launch_prefill_range_affine(const PrefillParams& p, cudaStream_t stream);
+cudaError_t launch_prefill_range_finish(const PrefillParams& p, cudaStream_t stream);
 bool prefill_chunk_supported(const PrefillParams& p);
 cudaError_t launch_prefill_chunk(const PrefillParams& p, cudaStream_t stream);
 // Per sequence the affine map of its token range, M [HV][K][K] and C [HV][V][K]

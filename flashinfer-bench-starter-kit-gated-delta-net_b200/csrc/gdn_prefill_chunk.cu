@@ -840,26 +840,40 @@ bool make_map(CUtensorMap* m, const void* base, int64_t tokens, int heads, int64
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Composition of the segment state maps (context parallelism inside the GPU):
+// Composition of the segment state maps (context parallelism):
 // S_in(s + 1) = S_in(s) M_s + C_s for s = 1 .. S - 1, fp32 on the CUDA cores; S_in(S) is
-// the sequence's final state (new_state).  The state rows are independent under the maps,
-// so a CTA carries its 32 rows of one (sequence, v-head) through every step without
-// synchronising with other CTAs.
+// the sequence's final state (new_state).  S_in(1) comes from kCpIn[0] (p.cp_combine 0: the
+// state leaving segment 0) or from p.state (3: the state entering a rank's range, also kept
+// in kCpIn[0]).  With p.cp_combine 1 / 2 the same fold from the identity without the C
+// terms / from zero gives the whole range's map M / C (into map_m / map_c).  The state rows
+// are independent under the maps, so a CTA carries its 32 rows of one (sequence, v-head)
+// through every step without synchronising with other CTAs.
 __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
   __shared__ __align__(16) float rows[32][kHeadDim];
   const int h = blockIdx.x, n = blockIdx.y, r0 = blockIdx.z * 32;
   const int tid = threadIdx.x, c = tid & 127, rh = (tid >> 7) * 16;  // column; first of 16 rows
-  const int S = p.cp_segments;
-  const float* in1 = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, 0, h) + (int64_t)r0 * kHeadDim;
-  for (int e = tid; e < 32 * kHeadDim / 4; e += 256)
-    reinterpret_cast<float4*>(&rows[0][0])[e] = reinterpret_cast<const float4*>(in1)[e];
+  const int S = p.cp_segments, mode = p.cp_combine;
+  float* in0 = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, 0, h) + (int64_t)r0 * kHeadDim;
+  if (mode == 0 || mode == 3) {
+    const float* src = mode == 0 ? in0
+                       : p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh + (int64_t)r0 * kHeadDim
+                                 : nullptr;  // zero incoming state
+    for (int e = tid; e < 32 * kHeadDim / 4; e += 256) {
+      const float4 x = src ? reinterpret_cast<const float4*>(src)[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float4*>(&rows[0][0])[e] = x;
+      if (mode == 3) reinterpret_cast<float4*>(in0)[e] = x;  // S_in(1), read by the output correction
+    }
+  } else {
+    for (int e = tid; e < 32 * kHeadDim; e += 256)
+      rows[e / kHeadDim][e % kHeadDim] = (mode == 1 && r0 + e / kHeadDim == e % kHeadDim) ? 1.f : 0.f;
+  }
   __syncthreads();
   for (int sg = 1; sg <= S - 1; ++sg) {
     const float* M = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpMap, n, sg - 1, h);
     const float* C = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpOff, n, sg - 1, h) + (int64_t)r0 * kHeadDim;
     float acc[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = C[(rh + r) * kHeadDim + c];
+    for (int r = 0; r < 16; ++r) acc[r] = mode == 1 ? 0.f : C[(rh + r) * kHeadDim + c];
 #pragma unroll 2
     for (int k = 0; k < kHeadDim; k += 4) {
       const float m0 = M[(k + 0) * kHeadDim + c], m1 = M[(k + 1) * kHeadDim + c];
@@ -874,13 +888,18 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
       }
     }
     __syncthreads();  // every thread has read the rows of S_in(sg)
-    float* out = (sg < S - 1 ? p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, sg, h)
-                             : p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh) +
-                 (int64_t)r0 * kHeadDim;
+    float* out = nullptr;
+    if (sg < S - 1) {
+      if (mode == 0 || mode == 3) out = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, sg, h);
+    } else {
+      out = mode == 1   ? p.map_m + (size_t)n * p.m_sn + (size_t)h * p.m_sh
+            : mode == 2 ? p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh
+                        : p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh;
+    }
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       rows[rh + r][c] = acc[r];
-      out[(rh + r) * kHeadDim + c] = acc[r];
+      if (out) out[(int64_t)(r0 + rh + r) * kHeadDim + c] = acc[r];
     }
     __syncthreads();
   }
@@ -1410,6 +1429,29 @@ cudaError_t launch_prefill_state_map(const PrefillParams& p, cudaStream_t stream
   return cudaGetLastError();
 }
 
+namespace {
+// The output correction of segments 1 .. S - 1 (q.cp_w0: segment 0's share of the chunks);
+// each CTA corrects ~16 chunks of one segment.
+cudaError_t launch_correct(PrefillParams q, const CUtensorMap& mphi_ld, const CUtensorMap& mo, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    e = cudaFuncSetAttribute(prefill_correct_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)corr::kSmAlloc);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int S = q.cp_segments;
+  const int64_t seg_chunks = (q.T / q.N / kC) * (1024 - q.cp_w0) / 1024 / (S - 1);
+  q.cp_parts = (int)(seg_chunks / 16 < 1 ? 1 : (seg_chunks / 16 > 64 ? 64 : seg_chunks / 16));
+  prefill_correct_kernel<<<dim3(q.HV, q.N, (S - 1) * q.cp_parts), corr::kThreads, corr::kSmAlloc, stream>>>(
+      mphi_ld, mo, q);
+  return cudaGetLastError();
+}
+}  // namespace
+
 cudaError_t launch_prefill_chunk(const PrefillParams& p_in, cudaStream_t stream) {
   if (p_in.N == 0) return cudaSuccess;
   PrefillParams p = p_in;
@@ -1450,22 +1492,94 @@ cudaError_t launch_prefill_chunk(const PrefillParams& p_in, cudaStream_t stream)
   if (e != cudaSuccess) return e;
   e = launch_prefill_combine(q, stream);
   if (e != cudaSuccess) return e;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    e = cudaFuncSetAttribute(prefill_correct_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)corr::kSmAlloc);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  return launch_correct(q, mphi_ld, mo, stream);
+}
+
+// ---- context parallelism across GPUs: a later token range of each sequence ----
+
+int prefill_range_segments(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  // S - 1 map-pair segments (segment 0 is empty): forced by the segment flag (n pairs), else
+  // the count k in [1, 8] minimising waves(2 c k) / k (+ ~2 chunks per CTA), with at least
+  // 4 chunks per segment on average
+  const int req = (int)((flags >> kPrefillSegmentsShift) & 15u);
+  if (req >= 1) return req + 1;
+  const int64_t chains = (int64_t)num_seqs * num_v_heads;
+  if (chains <= 0 || num_seqs <= 0) return 2;
+  const double avg_chunks = (double)total_tokens / (double)num_seqs / kC;
+  const int64_t sms = device_sm_count();
+  double best = 1e30;
+  int best_k = 1;
+  for (int k = 1; k <= 8; ++k) {
+    if (k > 1 && avg_chunks < 4.0 * k) break;
+    const double waves = (double)((2 * chains * k + sms - 1) / sms);
+    const double cost = waves * (1.0 / k + (avg_chunks > 0 ? 2.0 / avg_chunks : 0.0));
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_k = k;
+    }
   }
-  // each CTA corrects ~16 chunks of one segment
-  const int64_t seg_chunks = (p.T / p.N / kC) * (1024 - plan.w0) / 1024 / (S - 1);
-  q.cp_parts = (int)(seg_chunks / 16 < 1 ? 1 : (seg_chunks / 16 > 64 ? 64 : seg_chunks / 16));
-  prefill_correct_kernel<<<dim3(p.HV, p.N, (S - 1) * q.cp_parts), corr::kThreads, corr::kSmAlloc, stream>>>(
-      mphi_ld, mo, q);
-  return cudaGetLastError();
+  return best_k + 1;
+}
+
+size_t prefill_range_workspace_bytes(int num_seqs, int64_t total_tokens, int num_v_heads, uint32_t flags) {
+  if (num_seqs <= 0 || num_v_heads <= 0) return 0;
+  const int S = prefill_range_segments(num_seqs, total_tokens, num_v_heads, flags);
+  return align256(chunk_records_bytes(num_seqs, total_tokens, num_v_heads)) +
+         align256(cp_states_bytes(num_seqs, num_v_heads, S)) +
+         (size_t)total_tokens * (size_t)num_v_heads * kHeadDim * sizeof(__nv_bfloat16);
+}
+
+namespace {
+// The range's parameters: segment 0 empty (w0 = 0), S - 1 map-pair segments, the
+// scratch and Phi in the workspace after the records.
+PrefillParams range_params(const PrefillParams& p) {
+  PrefillParams q = p;
+  const int S = prefill_range_segments(p.N, p.T, p.HV, p.flags);
+  unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+  const size_t states_at = align256(chunk_records_bytes(p.N, p.T, p.HV));
+  q.cp_segments = S;
+  q.cp_w0 = 0;
+  q.cp_pass = 1;
+  q.cp_scratch = reinterpret_cast<float*>(ws + states_at);
+  q.cp_phi = reinterpret_cast<__nv_bfloat16*>(ws + states_at + align256(cp_states_bytes(p.N, p.HV, S)));
+  return q;
+}
+}  // namespace
+
+cudaError_t launch_prefill_range_affine(const PrefillParams& p, cudaStream_t stream) {
+  if (p.N == 0) return cudaSuccess;
+  PrefillParams q = range_params(p);
+  q.state = nullptr;  // segment 0 is empty; the map pairs start from the identity and from zero
+  q.new_state = nullptr;
+  CUtensorMap mk, mq, mv, mo, mphi_st;
+  cudaError_t e = prefill_setup(q, stream, &mk, &mq, &mv, &mo);
+  if (e != cudaSuccess) return e;
+  if (!make_map(&mphi_st, q.cp_phi, p.T, p.HV, (int64_t)p.HV * kHeadDim, kHeadDim, 128, false))
+    return cudaErrorInvalidValue;
+  prefill_chunk_kernel<<<dim3(p.HV, p.N, 2 * q.cp_segments - 1), kThreads, kSmAlloc, stream>>>(mk, mq, mv, mo,
+                                                                                              mphi_st, q);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  for (int mode = 1; mode <= 2; ++mode) {  // the range's M, then its C
+    q.cp_combine = mode;
+    e = launch_prefill_combine(q, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_prefill_range_finish(const PrefillParams& p, cudaStream_t stream) {
+  if (p.N == 0) return cudaSuccess;
+  PrefillParams q = range_params(p);
+  q.cp_combine = 3;  // from the incoming state p.state to new_state, keeping every segment's start
+  cudaError_t e = launch_prefill_combine(q, stream);
+  if (e != cudaSuccess) return e;
+  if (p.T <= 0) return cudaSuccess;
+  CUtensorMap mo, mphi_ld;
+  if (!make_map(&mo, p.out, p.T, p.HV, p.o_st, p.o_sh, 128, false) ||
+      !make_map(&mphi_ld, q.cp_phi, p.T, p.HV, (int64_t)p.HV * kHeadDim, kHeadDim, 64, true))
+    return cudaErrorInvalidValue;
+  return launch_correct(q, mphi_ld, mo, stream);
 }
 
 }  // namespace gdn

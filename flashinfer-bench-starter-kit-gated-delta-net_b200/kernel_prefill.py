@@ -180,3 +180,81 @@ def state_map(q, k, v, A_log, a, dt_bias, b, cu_seqlens, map_m=None, map_c=None,
                                    N, T, HQ, HV, D, ptr(workspace), ws_bytes, flags, stream_handle(q.device))
     _lib.check(rc)
     return map_m, map_c
+
+
+class RangeHandle:
+    """What ``range_affine`` leaves for ``range_finish``: the range's outputs from a zero
+    initial state (``out``, completed in place by ``range_finish``), its map
+    (``map_m``, ``map_c``) and the workspace holding its segments' maps and homogeneous
+    outputs (owned by the handle)."""
+
+    def __init__(self, out, map_m, map_c, workspace, cu, sizes, flags):
+        self.out, self.map_m, self.map_c, self.workspace = out, map_m, map_c, workspace
+        self.cu, self.sizes, self.flags = cu, sizes, flags
+
+
+def range_affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale, *, segments: int = 0) -> RangeHandle:
+    """First half of the prefill of a later token range of each sequence (context
+    parallelism across GPUs; C ABI ``gdn_prefill_range_affine``): the range's outputs from
+    a zero initial state and its affine map ``S_out = S_in @ M + C``, before ``S_in`` is
+    known.  ``range_finish`` completes the outputs and gives ``S_out`` once it is.  No
+    token runs twice.  ``segments`` = map-pair segments per range run on separate SMs
+    (0 = the library decides).  No counterpart in the reference."""
+    if not 0 <= int(segments) <= 15:
+        raise ValueError(f"segments must be in [0, 15], got {segments}")
+    T, HQ, D = q.shape
+    HV = v.shape[1]
+    N = cu_seqlens.shape[0] - 1
+    check_cuda(q, k, v, A_log, a, dt_bias, b)
+    if cu_seqlens.device != q.device:
+        raise ValueError("cu_seqlens must be on the same device as q")
+    if cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
+    if scale is None or scale == 0.0:
+        scale = 1.0 / math.sqrt(D)
+    q, k, v = inner_contig(q), inner_contig(k), inner_contig(v)
+    a, b = inner_contig(a), inner_contig(b)
+    A_log, dt_bias, cu = A_log.contiguous(), dt_bias.contiguous(), cu_seqlens.contiguous()
+    out = torch.empty(T, HV, D, dtype=torch.bfloat16, device=q.device)
+    map_m = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
+    map_c = torch.empty(N, HV, D, D, dtype=torch.float32, device=q.device)
+    lib = _lib.library()
+    flags = _lib.GDN_FLAG_RANGE_AFFINE | _lib.GDN_PREFILL_SEGMENTS(segments)
+    need = int(lib.gdn_prefill_workspace_size(N, T, HQ, HV, D, flags))
+    workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    rc = lib.gdn_prefill_range_affine(ptr(q), *seq_head_strides(q, 0, 1), ptr(k), *seq_head_strides(k, 0, 1),
+                                      ptr(v), *seq_head_strides(v, 0, 1),
+                                      ptr(A_log), ptr(a), a.stride(0), ptr(dt_bias), ptr(b), b.stride(0),
+                                      ptr(cu), int(cu.dtype == torch.int64), float(scale),
+                                      ptr(out), *seq_head_strides(out, 0, 1),
+                                      ptr(map_m), *seq_head_strides(map_m, 0, 1),
+                                      ptr(map_c), *seq_head_strides(map_c, 0, 1),
+                                      N, T, HQ, HV, D, ptr(workspace), workspace.numel(), flags,
+                                      stream_handle(q.device))
+    _lib.check(rc)
+    return RangeHandle(out, map_m, map_c, workspace, cu, (N, T, HQ, HV, D), flags)
+
+
+def range_finish(handle: RangeHandle, state_in, new_state=None):
+    """Second half (C ABI ``gdn_prefill_range_finish``): given the state entering the range
+    (``state_in`` [N,HV,128,128] fp32, None = zero), completes ``handle.out`` in place
+    and returns ``(out, S_out)``."""
+    N, T, HQ, HV, D = handle.sizes
+    dev = handle.out.device
+    if new_state is None:
+        new_state = torch.empty(N, HV, D, D, dtype=torch.float32, device=dev)
+    for name, x in (("state_in", state_in), ("new_state", new_state)):
+        if x is not None and (x.device != dev or x.dtype != torch.float32 or tuple(x.shape) != (N, HV, D, D)):
+            raise ValueError(f"{name} must be a float32 [{N}, {HV}, {D}, {D}] tensor on {dev}")
+    if state_in is not None and not state_in.is_contiguous() and state_in is not new_state:
+        state_in = state_in.contiguous()
+    lib = _lib.library()
+    rc = lib.gdn_prefill_range_finish(ptr(handle.cu), int(handle.cu.dtype == torch.int64),
+                                      ptr(state_in), *(seq_head_strides(state_in, 0, 1) if state_in is not None
+                                                       else (0, 0)),
+                                      ptr(handle.out), *seq_head_strides(handle.out, 0, 1),
+                                      ptr(new_state), *seq_head_strides(new_state, 0, 1),
+                                      N, T, HQ, HV, D, ptr(handle.workspace), handle.workspace.numel(),
+                                      handle.flags, stream_handle(dev))
+    _lib.check(rc)
+    return handle.out, new_state

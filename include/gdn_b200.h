@@ -49,12 +49,18 @@ extern "C" {
 #define GDN_FLAG_PREFILL_SERIAL 0x2u /* prefill: use the token-serial kernel instead of the chunked
                                         tensor-core kernel (cross-checking; prefill only) */
 /* Prefill: split each sequence's chunks into n segments (2..15) that run on separate SMs
- * (context parallelism: per-segment affine state maps, composed, then the segments rerun
- * from their initial states).  0 = automatic (segments only when the (sequence, v-head)
- * chains leave most SMs idle and sequences are long), 1 = never.  Bits 8-11. */
+ * (context parallelism: segment 0 from the initial state; every later segment's affine
+ * state map and its outputs from a zero and from the identity state; the maps composed;
+ * the later segments' outputs corrected by their initial states).  0 = automatic
+ * (segments only when the (sequence, v-head) chains leave most SMs idle and sequences are
+ * long), 1 = never.  Bits 8-11.  gdn_prefill_range_affine / _finish: n map-pair segments
+ * (1..15) instead, 0 = automatic. */
 #define GDN_PREFILL_SEGMENTS(n) ((((uint32_t)(n)) & 15u) << 8)
 /* gdn_prefill_workspace_size: size the workspace of gdn_prefill_state_map instead. */
 #define GDN_FLAG_STATE_MAP 0x4u
+/* gdn_prefill_workspace_size: size the workspace of gdn_prefill_range_affine / _finish
+ * instead; those two calls take it in their flags as well. */
+#define GDN_FLAG_RANGE_AFFINE 0x8u
 /* gdn_decode self-test of the device-side failure path: every thread of the launch waits
  * on a barrier that nothing completes, gives up after 1 ms, records
  * GDN_DEVERR_WAIT_TIMEOUT and returns; out and new_state are not written.  No copy or
@@ -206,6 +212,49 @@ GDN_API int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_s
                 const void* cu_seqlens, int32_t cu_seqlens_is_int64,
                 float* map_m, int64_t map_m_stride_n, int64_t map_m_stride_h,
                 float* map_c, int64_t map_c_stride_n, int64_t map_c_stride_h,
+                int32_t num_seqs, int64_t total_tokens,
+                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                void* workspace, size_t workspace_bytes,
+                uint32_t flags, void* stream);
+
+/*
+ * Context parallelism across GPUs for a rank that holds a later token range of each
+ * sequence (no counterpart in the reference, whose prefill is token-serial).  The range's
+ * outputs and final state are affine in the state S_in entering it, which the rank learns
+ * only from the other ranks' maps, so its prefill is split around that exchange:
+ *   gdn_prefill_range_affine  (before): writes out = the range's outputs from a zero initial
+ *     state and the range's map, S_out = S_in M + C (map_m, map_c as in
+ *     gdn_prefill_state_map); keeps in the workspace the homogeneous outputs (those of the
+ *     range run from the identity with v taken as 0) and the maps of its segments.
+ *   gdn_prefill_range_finish  (after): given S_in (state, NULL = zero), adds S_in's share to
+ *     out (the same buffer) and writes S_out to new_state (may alias state).
+ * No token runs twice.  Inputs as gdn_prefill (q/k/v and out rows 16-byte aligned); q and
+ * k are used as given (GDN_FLAG_QK_L2NORM is not supported here).  Both calls take the same
+ * num_seqs, total_tokens, head counts, flags (GDN_FLAG_RANGE_AFFINE, optionally
+ * GDN_PREFILL_SEGMENTS(n)) and workspace: at least
+ * gdn_prefill_workspace_size(..., GDN_FLAG_RANGE_AFFINE | flags) bytes, 16-byte aligned,
+ * left untouched between them.
+ */
+GDN_API int gdn_prefill_range_affine(const void* q, int64_t q_stride_t, int64_t q_stride_h,
+                const void* k, int64_t k_stride_t, int64_t k_stride_h,
+                const void* v, int64_t v_stride_t, int64_t v_stride_h,
+                const float* A_log,
+                const void* a, int64_t a_stride_t,
+                const float* dt_bias,
+                const void* b, int64_t b_stride_t,
+                const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                float scale,
+                void* out, int64_t out_stride_t, int64_t out_stride_h,
+                float* map_m, int64_t map_m_stride_n, int64_t map_m_stride_h,
+                float* map_c, int64_t map_c_stride_n, int64_t map_c_stride_h,
+                int32_t num_seqs, int64_t total_tokens,
+                int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
+                void* workspace, size_t workspace_bytes,
+                uint32_t flags, void* stream);
+GDN_API int gdn_prefill_range_finish(const void* cu_seqlens, int32_t cu_seqlens_is_int64,
+                const float* state, int64_t state_stride_n, int64_t state_stride_h,
+                void* out, int64_t out_stride_t, int64_t out_stride_h,
+                float* new_state, int64_t new_state_stride_n, int64_t new_state_stride_h,
                 int32_t num_seqs, int64_t total_tokens,
                 int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim,
                 void* workspace, size_t workspace_bytes,

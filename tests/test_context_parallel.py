@@ -59,7 +59,16 @@ def _oracle_ops(cp):
                            cu.numpy(), None)
         return torch.from_numpy(np.ascontiguousarray(m)), torch.from_numpy(np.ascontiguousarray(c))
 
-    return cp.Ops(prefill=prefill, state_map=state_map, compose=lambda S, M, C: torch.matmul(S, M) + C)
+    def affine(q, k, v, A_log, a, dt_bias, b, cu, scale):
+        # the range's map now; its outputs once the incoming state is known (a rerun here)
+        m, c = state_map(q, k, v, A_log, a, dt_bias, b, cu)
+        return (q, k, v, A_log, a, dt_bias, b, cu, scale), m, c
+
+    def finish(handle, s_in):
+        q, k, v, A_log, a, dt_bias, b, cu, scale = handle
+        return prefill(q, k, v, s_in, A_log, a, dt_bias, b, cu, scale)
+
+    return cp.Ops(prefill=prefill, affine=affine, finish=finish, compose=lambda S, M, C: torch.matmul(S, M) + C)
 
 
 def _cp_worker(rank, world, port, q):

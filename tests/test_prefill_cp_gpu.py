@@ -156,7 +156,8 @@ def test_state_map_automatic_segments_one_long_sequence(gdn):
 
 def test_context_parallel_steps_on_one_gpu(gdn):
     """The three ranks of a context-parallel prefill emulated on one device with the
-    CUDA operators (maps, fold, reruns) against the oracle's whole sequences."""
+    CUDA operators (rank 0's prefill, the other ranks' affine passes, the fold, their
+    finishes) against the oracle's whole sequences."""
     cp = gdn.context_parallel
     ops = cp.cuda_ops()
     lens, world = [2000, 513, 64], 3
@@ -167,13 +168,14 @@ def test_context_parallel_steps_on_one_gpu(gdn):
     gate = lambda L: (L["A_log"], L["a"], L["dt_bias"], L["b"], L["cu_seqlens"])  # noqa: E731
     outs = [None] * world
     outs[0], s = ops.prefill(*(locs[0][x] for x in keys), dev["state"], *gate(locs[0]), dev["scale"])
-    pairs = [(torch.zeros_like(s), s)] + [ops.state_map(*(locs[r][x] for x in keys), *gate(locs[r]))
-                                          for r in range(1, world)]
+    affine = [None] + [ops.affine(*(locs[r][x] for x in keys), *gate(locs[r]), dev["scale"])
+                       for r in range(1, world)]
+    pairs = [(torch.zeros_like(s), s)] + [(affine[r][1], affine[r][2]) for r in range(1, world)]
     for r in range(1, world):
         s_in = torch.zeros_like(s)
         for j in range(r):
             s_in = ops.compose(s_in, *pairs[j])
-        outs[r], s_r = ops.prefill(*(locs[r][x] for x in keys), s_in, *gate(locs[r]), dev["scale"])
+        outs[r], s_r = ops.finish(affine[r][0], s_in)
     torch.cuda.synchronize()
     o_ref, s_ref = oracle_prefill(inp)
     o_ref = ref.bf16_bits_to_f32(o_ref)
@@ -188,3 +190,59 @@ def test_context_parallel_steps_on_one_gpu(gdn):
     np.testing.assert_allclose(out, o_ref, **OUT_TOL)
     ok, err = state_close(s_r.cpu().numpy(), s_ref, 1e-3)
     assert ok, err
+
+
+def _cut(inp, cuts):
+    """Head [0, x) and tail [x, L) of every sequence as two prefill input dicts."""
+    cu = inp["cu_seqlens"].cpu().tolist()
+    head_idx, tail_idx, head_cu, tail_cu = [], [], [0], [0]
+    for i, x in enumerate(cuts):
+        lo, hi = cu[i], cu[i + 1]
+        head_idx.append(torch.arange(lo, lo + x))
+        tail_idx.append(torch.arange(lo + x, hi))
+        head_cu.append(head_cu[-1] + x)
+        tail_cu.append(tail_cu[-1] + hi - lo - x)
+    parts = []
+    for idx, c in ((torch.cat(head_idx), head_cu), (torch.cat(tail_idx), tail_cu)):
+        d = dict(inp)
+        idx = idx.to(inp["q"].device)
+        for key in ("q", "k", "v", "a", "b"):
+            d[key] = inp[key].index_select(0, idx).contiguous()
+        d["cu_seqlens"] = torch.tensor(c, dtype=inp["cu_seqlens"].dtype, device=inp["cu_seqlens"].device)
+        parts.append((d, idx))
+    return parts
+
+
+@pytest.mark.parametrize("segments", [0, 1, 3])
+def test_range_affine_finish_matches_whole_sequences(gdn, segments):
+    """A later token range of every sequence run as ``range_affine`` (its outputs from a
+    zero state and its map, before the state entering it is known) and ``range_finish``
+    (given that state): the outputs and final states of the whole-sequence prefill, and
+    the map of ``state_map``.  Empty, sub-chunk and partial-chunk ranges; automatic and
+    forced segment counts; the finish in place."""
+    lens = [0, 37, 700, 2061, 192, 1500]
+    inp = to_dev(gdn.workloads.prefill_inputs(lens, seed=360 + segments))
+    o_all, s_all = gdn.kernel_prefill.run(**inp, segments=1)
+    (head, _), (tail, tail_idx) = _cut(inp, [64 * ((L // 64) // 2) for L in lens])
+    _, s_mid = gdn.kernel_prefill.run(**head, segments=1)
+    args = [tail[k] for k in ("q", "k", "v", "A_log", "a", "dt_bias", "b", "cu_seqlens", "scale")]
+    h = gdn.kernel_prefill.range_affine(*args, segments=segments)
+    m_ref, c_ref = gdn.kernel_prefill.state_map(*args[:8], segments=1)
+    torch.cuda.synchronize()
+    # M is dimensionless (identity scale); where the decay has all but emptied it, the segmented
+    # and single-chain products differ relative to its size but not to the identity's
+    assert float((h.map_m - m_ref).abs().max()) <= 1e-4
+    ok, err = state_close(h.map_c.cpu().numpy(), c_ref.cpu().numpy(), 1e-3)
+    assert ok, err
+    composed = torch.matmul(s_mid, h.map_m) + h.map_c  # what the other ranks' exchange uses
+    ok, err = state_close(composed.cpu().numpy(), s_all.cpu().numpy(), 1e-3)
+    assert ok, err
+    s_in = s_mid.clone()
+    out, s_end = gdn.kernel_prefill.range_finish(h, s_in, new_state=s_in)  # in place
+    torch.cuda.synchronize()
+    assert s_end is s_in
+    np.testing.assert_allclose(out.float().cpu().numpy(), o_all[tail_idx].float().cpu().numpy(), **OUT_TOL)
+    ok, err = state_close(s_end.cpu().numpy(), s_all.cpu().numpy(), 1e-3)
+    assert ok, err
+    assert torch.equal(s_end[0], s_mid[0])  # empty sequence: the state passes through
+    assert gdn._lib.device_error() == 0
