@@ -88,6 +88,7 @@ SIGNATURES = {
                                   _P, _SZ, _U32, _P], ctypes.c_int),
     "gdn_prefill_range_finish": ([_P, _I32,                                         # cu_seqlens
                                   _P, _I64, _I64,                                   # state (S_in)
+                                  _P, _I32,                                         # prev_maps, count
                                   _P, _I64, _I64,                                   # out
                                   _P, _I64, _I64,                                   # new_state
                                   _I32, _I64, _I32, _I32, _I32,                     # N, T, HQ, HV, D

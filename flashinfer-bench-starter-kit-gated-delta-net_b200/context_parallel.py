@@ -14,16 +14,16 @@ the run from the identity).  So:
 2. one ``all_gather`` of ``[2, N, HV, 128, 128]`` fp32 per rank: rank 0 sends
    ``(0, S_end)``, rank r sends ``(M_r, C_r)`` (the one exchange step of d x d
    matrices per range);
-3. rank r > 0 folds ``S <- S @ M_j + C_j`` over j < r from ``S = 0`` (rank 0's pair
-   gives ``S_end``) to get the state entering its ranges, and ``range_finish`` adds that
-   state's share to its outputs and gives the state leaving them (no token runs twice);
+3. rank r > 0 hands the pairs of ranks j < r to ``range_finish``, which folds
+   ``S <- S @ M_j + C_j`` from ``S = 0`` on the GPU (rank 0's pair gives ``S_end``) to get
+   the state entering its ranges, adds that state's share to its outputs and gives the
+   state leaving them (no token runs twice);
 4. the last rank's final state is broadcast, so every rank returns the sequences'
    final state.
 
 Both rank 0's prefill and the other ranks' affine pass cut their ranges into segments on
-separate SMs (one long 32-head sequence: rank 0's prefill ~0.45 and an affine pass ~0.5 of
-one chain per token, the finish ~0.1 more after the exchange), so rank 0's range is
-weighted ``FIRST_RANK_WEIGHT`` = 1.2 times the others'.  The reference has no long-context
+separate SMs; measured on one long 32-head sequence, rank 0's prefill of a range takes
+about as long as an affine pass of an equal one, so ``FIRST_RANK_WEIGHT`` is 1.  The reference has no long-context
 parallelism (its prefill is token-serial per sequence, ``solution/triton/kernel_prefill.py:88``).
 
 ``split_ranges``/``local_inputs`` cut a global varlen batch into rank-local inputs:
@@ -38,7 +38,7 @@ import torch
 import torch.distributed as dist
 
 CHUNK = 64
-FIRST_RANK_WEIGHT = 1.2
+FIRST_RANK_WEIGHT = 1.0
 
 
 def split_ranges(seqlens, world: int, first_weight: float = FIRST_RANK_WEIGHT) -> list[list[tuple[int, int]]]:
@@ -88,21 +88,20 @@ class Ops:
     implementation to exercise the exchange on gloo ranks)."""
     prefill: Callable  # (q,k,v,state,A_log,a,dt_bias,b,cu_seqlens,scale) -> (out, final_state)
     affine: Callable  # (q,k,v,A_log,a,dt_bias,b,cu_seqlens,scale) -> (handle, M, C)
-    finish: Callable  # (handle, S_in) -> (out, final_state)
-    compose: Callable  # (S, M, C) -> S @ M + C   (per sequence and v-head, fp32)
+    finish: Callable  # (handle, prev [R, 2, N, HV, K, K]: the preceding ranges' (M, C)) -> (out, final_state)
 
 
 def cuda_ops() -> Ops:
     from . import kernel_prefill
 
-    def compose(S, M, C):
-        return torch.baddbmm(C.flatten(0, 1), S.flatten(0, 1), M.flatten(0, 1)).view_as(C)
-
     def affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale):
         h = kernel_prefill.range_affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale)
         return h, h.map_m, h.map_c
 
-    return Ops(prefill=kernel_prefill.run, affine=affine, finish=kernel_prefill.range_finish, compose=compose)
+    def finish(handle, prev):
+        return kernel_prefill.range_finish(handle, prev_maps=prev)
+
+    return Ops(prefill=kernel_prefill.run, affine=affine, finish=finish)
 
 
 def prefill_context_parallel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *, group=None,
@@ -124,13 +123,10 @@ def prefill_context_parallel(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, s
     else:
         handle, m, c = ops.affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale)
         pair = torch.stack([m, c])
-    pairs = [torch.empty(2, N, HV, D, D, dtype=torch.float32, device=dev) for _ in range(world)]
-    dist.all_gather(pairs, pair.contiguous(), group=group)
+    pairs = torch.empty(world, 2, N, HV, D, D, dtype=torch.float32, device=dev)
+    dist.all_gather(list(pairs.unbind(0)), pair.contiguous(), group=group)  # into views of one tensor
     if rank > 0:
-        s_in = torch.zeros(N, HV, D, D, dtype=torch.float32, device=dev)
-        for j in range(rank):
-            s_in = ops.compose(s_in, pairs[j][0], pairs[j][1])
-        out, s_end = ops.finish(handle, s_in)
+        out, s_end = ops.finish(handle, pairs[:rank])
     final = s_end.contiguous() if rank == world - 1 else torch.empty(N, HV, D, D, dtype=torch.float32, device=dev)
     src = dist.get_global_rank(group, world - 1) if group is not None else world - 1
     dist.broadcast(final, src=src, group=group)

@@ -508,7 +508,8 @@ int gdn_prefill_range_affine(const void* q, int64_t q_stride_t, int64_t q_stride
 }
 
 int gdn_prefill_range_finish(const void* cu_seqlens, int32_t cu_seqlens_is_int64, const float* state,
-                             int64_t state_stride_n, int64_t state_stride_h, void* out, int64_t out_stride_t,
+                             int64_t state_stride_n, int64_t state_stride_h, const float* prev_maps,
+                             int32_t num_prev_maps, void* out, int64_t out_stride_t,
                              int64_t out_stride_h, float* new_state, int64_t new_state_stride_n,
                              int64_t new_state_stride_h, int32_t num_seqs, int64_t total_tokens,
                              int32_t num_qk_heads, int32_t num_v_heads, int32_t head_dim, void* workspace,
@@ -528,6 +529,12 @@ int gdn_prefill_range_finish(const void* cu_seqlens, int32_t cu_seqlens_is_int64
     if ((reinterpret_cast<uintptr_t>(out) & 15) || (out_stride_t & 7) || (out_stride_h & 7))
       return fail(GDN_ERR_UNSUPPORTED, "out rows must be 16-byte aligned (base and strides)");
   }
+  if (num_prev_maps < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "num_prev_maps must be >= 0");
+  if (num_prev_maps > 0) {
+    if (state) return fail(GDN_ERR_INVALID_ARGUMENT, "give either state or prev_maps, not both");
+    if (!prev_maps || (reinterpret_cast<uintptr_t>(prev_maps) & 15))
+      return fail(GDN_ERR_INVALID_ARGUMENT, "prev_maps must be a 16-byte aligned device pointer");
+  }
   rc = check_state_pair(state, state_stride_n, state_stride_h, new_state, new_state_stride_n, new_state_stride_h,
                         num_seqs, num_v_heads);
   if (rc) return rc;
@@ -536,6 +543,8 @@ int gdn_prefill_range_finish(const void* cu_seqlens, int32_t cu_seqlens_is_int64
     return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes (16-byte aligned) required (got %zu)", need,
                 workspace_bytes);
   gdn::PrefillParams p;
+  p.cp_prev = prev_maps;
+  p.cp_prev_count = num_prev_maps;
   p.cu_seqlens = cu_seqlens;
   p.cu_is_int64 = cu_seqlens_is_int64 ? 1 : 0;
   p.state = state;

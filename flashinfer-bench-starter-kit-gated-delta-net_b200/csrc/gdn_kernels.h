@@ -78,6 +78,10 @@ struct PrefillParams {
   // state (a range's incoming state, also copied to kCpIn[0]), both ending in new_state;
   // 1 = the range's M (from the identity, no C) into map_m, 2 = its C (from zero) into map_c
   int cp_combine = 0;
+  // cp_combine 3: when cp_prev_count > 0 the incoming state is the fold S = 0,
+  // S <- S M_j + C_j over cp_prev [cp_prev_count][2 (M, C)][N][HV][128][128] (p.state unused)
+  const float* cp_prev = nullptr;
+  int cp_prev_count = 0;
   float* cp_scratch = nullptr;
   __nv_bfloat16* cp_phi = nullptr;
   // GDN_FLAG_QK_L2NORM: per (token, q/k head) (1 / |q|, log2 (1 / |q|)), [T][HQ] (workspace)

@@ -848,46 +848,68 @@ bool make_map(CUtensorMap* m, const void* base, int64_t tokens, int heads, int64
 // terms / from zero gives the whole range's map M / C (into map_m / map_c).  The state rows
 // are independent under the maps, so a CTA carries its 32 rows of one (sequence, v-head)
 // through every step without synchronising with other CTAs.
+// rows <- rows M + C (C optional) for a CTA's 32 state rows r0 .. r0 + 31 (thread: column c
+// of 16 rows rh ..), then stored to out when given; M [128][128] and C's rows in global memory.
+__device__ __forceinline__ void fold_rows(float (*rows)[kHeadDim], const float* M, const float* C, float* out, int r0,
+                                          int c, int rh) {
+  float acc[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) acc[r] = C ? C[(int64_t)(r0 + rh + r) * kHeadDim + c] : 0.f;
+#pragma unroll 2
+  for (int k = 0; k < kHeadDim; k += 4) {
+    const float m0 = M[(k + 0) * kHeadDim + c], m1 = M[(k + 1) * kHeadDim + c];
+    const float m2 = M[(k + 2) * kHeadDim + c], m3 = M[(k + 3) * kHeadDim + c];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const float4 x = *reinterpret_cast<const float4*>(&rows[rh + r][k]);
+      acc[r] = fmaf(x.x, m0, acc[r]);
+      acc[r] = fmaf(x.y, m1, acc[r]);
+      acc[r] = fmaf(x.z, m2, acc[r]);
+      acc[r] = fmaf(x.w, m3, acc[r]);
+    }
+  }
+  __syncthreads();  // every thread has read the rows
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    rows[rh + r][c] = acc[r];
+    if (out) out[(int64_t)(r0 + rh + r) * kHeadDim + c] = acc[r];
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
   __shared__ __align__(16) float rows[32][kHeadDim];
   const int h = blockIdx.x, n = blockIdx.y, r0 = blockIdx.z * 32;
   const int tid = threadIdx.x, c = tid & 127, rh = (tid >> 7) * 16;  // column; first of 16 rows
   const int S = p.cp_segments, mode = p.cp_combine;
-  float* in0 = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, 0, h) + (int64_t)r0 * kHeadDim;
-  if (mode == 0 || mode == 3) {
-    const float* src = mode == 0 ? in0
+  float* in0 = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, 0, h);
+  if (mode == 3 && p.cp_prev_count > 0) {
+    // the state entering the range: S = 0, S <- S M_j + C_j over the preceding ranges' maps
+    for (int e = tid; e < 32 * kHeadDim; e += 256) rows[e / kHeadDim][e % kHeadDim] = 0.f;
+    __syncthreads();
+    for (int j = 0; j < p.cp_prev_count; ++j) {
+      const float* M = p.cp_prev + (((int64_t)(2 * j) * p.N + n) * p.HV + h) * kStateFloats;
+      const float* C = p.cp_prev + (((int64_t)(2 * j + 1) * p.N + n) * p.HV + h) * kStateFloats;
+      fold_rows(rows, M, C, j + 1 == p.cp_prev_count ? in0 : nullptr, r0, c, rh);  // S_in(1) kept
+    }
+  } else if (mode == 0 || mode == 3) {
+    const float* src = mode == 0 ? in0 + (int64_t)r0 * kHeadDim
                        : p.state ? p.state + (size_t)n * p.s_sn + (size_t)h * p.s_sh + (int64_t)r0 * kHeadDim
                                  : nullptr;  // zero incoming state
     for (int e = tid; e < 32 * kHeadDim / 4; e += 256) {
       const float4 x = src ? reinterpret_cast<const float4*>(src)[e] : make_float4(0.f, 0.f, 0.f, 0.f);
       reinterpret_cast<float4*>(&rows[0][0])[e] = x;
-      if (mode == 3) reinterpret_cast<float4*>(in0)[e] = x;  // S_in(1), read by the output correction
+      if (mode == 3) reinterpret_cast<float4*>(in0 + (int64_t)r0 * kHeadDim)[e] = x;  // S_in(1), for the correction
     }
+    __syncthreads();
   } else {
     for (int e = tid; e < 32 * kHeadDim; e += 256)
       rows[e / kHeadDim][e % kHeadDim] = (mode == 1 && r0 + e / kHeadDim == e % kHeadDim) ? 1.f : 0.f;
+    __syncthreads();
   }
-  __syncthreads();
   for (int sg = 1; sg <= S - 1; ++sg) {
     const float* M = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpMap, n, sg - 1, h);
-    const float* C = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpOff, n, sg - 1, h) + (int64_t)r0 * kHeadDim;
-    float acc[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = mode == 1 ? 0.f : C[(rh + r) * kHeadDim + c];
-#pragma unroll 2
-    for (int k = 0; k < kHeadDim; k += 4) {
-      const float m0 = M[(k + 0) * kHeadDim + c], m1 = M[(k + 1) * kHeadDim + c];
-      const float m2 = M[(k + 2) * kHeadDim + c], m3 = M[(k + 3) * kHeadDim + c];
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const float4 x = *reinterpret_cast<const float4*>(&rows[rh + r][k]);
-        acc[r] = fmaf(x.x, m0, acc[r]);
-        acc[r] = fmaf(x.y, m1, acc[r]);
-        acc[r] = fmaf(x.z, m2, acc[r]);
-        acc[r] = fmaf(x.w, m3, acc[r]);
-      }
-    }
-    __syncthreads();  // every thread has read the rows of S_in(sg)
+    const float* C = mode == 1 ? nullptr : p.cp_scratch + cp_offset(p.N, p.HV, S, kCpOff, n, sg - 1, h);
     float* out = nullptr;
     if (sg < S - 1) {
       if (mode == 0 || mode == 3) out = p.cp_scratch + cp_offset(p.N, p.HV, S, kCpIn, n, sg, h);
@@ -896,12 +918,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillParams p) {
             : mode == 2 ? p.map_c + (size_t)n * p.c_sn + (size_t)h * p.c_sh
                         : p.new_state + (size_t)n * p.n_sn + (size_t)h * p.n_sh;
     }
-#pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      rows[rh + r][c] = acc[r];
-      if (out) out[(int64_t)(r0 + rh + r) * kHeadDim + c] = acc[r];
-    }
-    __syncthreads();
+    fold_rows(rows, M, C, out, r0, c, rh);
   }
 }
 

@@ -235,10 +235,12 @@ def range_affine(q, k, v, A_log, a, dt_bias, b, cu_seqlens, scale, *, segments: 
     return RangeHandle(out, map_m, map_c, workspace, cu, (N, T, HQ, HV, D), flags)
 
 
-def range_finish(handle: RangeHandle, state_in, new_state=None):
-    """Second half (C ABI ``gdn_prefill_range_finish``): given the state entering the range
-    (``state_in`` [N,HV,128,128] fp32, None = zero), completes ``handle.out`` in place
-    and returns ``(out, S_out)``."""
+def range_finish(handle: RangeHandle, state_in=None, new_state=None, *, prev_maps=None):
+    """Second half (C ABI ``gdn_prefill_range_finish``): given the state entering the range,
+    completes ``handle.out`` in place and returns ``(out, S_out)``.  The state is
+    ``state_in`` [N,HV,128,128] fp32 (None = zero) or, with ``prev_maps``
+    [R,2,N,HV,128,128] fp32 (the (M, C) maps of the R preceding ranges; the first may be
+    (0, its final state)), their fold ``S = 0; S = S @ M_j + C_j``, done on the GPU."""
     N, T, HQ, HV, D = handle.sizes
     dev = handle.out.device
     if new_state is None:
@@ -246,12 +248,22 @@ def range_finish(handle: RangeHandle, state_in, new_state=None):
     for name, x in (("state_in", state_in), ("new_state", new_state)):
         if x is not None and (x.device != dev or x.dtype != torch.float32 or tuple(x.shape) != (N, HV, D, D)):
             raise ValueError(f"{name} must be a float32 [{N}, {HV}, {D}, {D}] tensor on {dev}")
+    count = 0
+    if prev_maps is not None:
+        if state_in is not None:
+            raise ValueError("give either state_in or prev_maps, not both")
+        if (prev_maps.device != dev or prev_maps.dtype != torch.float32 or prev_maps.dim() != 6
+                or tuple(prev_maps.shape[1:]) != (2, N, HV, D, D)):
+            raise ValueError(f"prev_maps must be a float32 [R, 2, {N}, {HV}, {D}, {D}] tensor on {dev}")
+        prev_maps = prev_maps.contiguous()
+        count = prev_maps.shape[0]
     if state_in is not None and not state_in.is_contiguous() and state_in is not new_state:
         state_in = state_in.contiguous()
     lib = _lib.library()
     rc = lib.gdn_prefill_range_finish(ptr(handle.cu), int(handle.cu.dtype == torch.int64),
                                       ptr(state_in), *(seq_head_strides(state_in, 0, 1) if state_in is not None
                                                        else (0, 0)),
+                                      ptr(prev_maps) if count else None, count,
                                       ptr(handle.out), *seq_head_strides(handle.out, 0, 1),
                                       ptr(new_state), *seq_head_strides(new_state, 0, 1),
                                       N, T, HQ, HV, D, ptr(handle.workspace), handle.workspace.numel(),

@@ -226,8 +226,12 @@ GDN_API int gdn_prefill_state_map(const void* q, int64_t q_stride_t, int64_t q_s
  *     state and the range's map, S_out = S_in M + C (map_m, map_c as in
  *     gdn_prefill_state_map); keeps in the workspace the homogeneous outputs (those of the
  *     range run from the identity with v taken as 0) and the maps of its segments.
- *   gdn_prefill_range_finish  (after): given S_in (state, NULL = zero), adds S_in's share to
- *     out (the same buffer) and writes S_out to new_state (may alias state).
+ *   gdn_prefill_range_finish  (after): given S_in, adds S_in's share to out (the same buffer)
+ *     and writes S_out to new_state (may alias state).  S_in is either state (NULL = zero)
+ *     or, with num_prev_maps > 0 and state NULL, the fold S = 0, S <- S M_j + C_j over the
+ *     preceding ranges' maps prev_maps [num_prev_maps][2 (M, C)][num_seqs][num_v_heads]
+ *     [head_dim][head_dim] fp32, contiguous (what an all_gather of (M, C) pairs holds;
+ *     the first range's pair may be (0, its final state)), done on the device.
  * No token runs twice.  Inputs as gdn_prefill (q/k/v and out rows 16-byte aligned); q and
  * k are used as given (GDN_FLAG_QK_L2NORM is not supported here).  Both calls take the same
  * num_seqs, total_tokens, head counts, flags (GDN_FLAG_RANGE_AFFINE, optionally
@@ -253,6 +257,7 @@ GDN_API int gdn_prefill_range_affine(const void* q, int64_t q_stride_t, int64_t 
                 uint32_t flags, void* stream);
 GDN_API int gdn_prefill_range_finish(const void* cu_seqlens, int32_t cu_seqlens_is_int64,
                 const float* state, int64_t state_stride_n, int64_t state_stride_h,
+                const float* prev_maps, int32_t num_prev_maps,
                 void* out, int64_t out_stride_t, int64_t out_stride_h,
                 float* new_state, int64_t new_state_stride_n, int64_t new_state_stride_h,
                 int32_t num_seqs, int64_t total_tokens,

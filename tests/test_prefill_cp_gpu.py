@@ -156,8 +156,8 @@ def test_state_map_automatic_segments_one_long_sequence(gdn):
 
 def test_context_parallel_steps_on_one_gpu(gdn):
     """The three ranks of a context-parallel prefill emulated on one device with the
-    CUDA operators (rank 0's prefill, the other ranks' affine passes, the fold, their
-    finishes) against the oracle's whole sequences."""
+    CUDA operators (rank 0's prefill, the other ranks' affine passes, their finishes from
+    the gathered maps) against the oracle's whole sequences."""
     cp = gdn.context_parallel
     ops = cp.cuda_ops()
     lens, world = [2000, 513, 64], 3
@@ -170,12 +170,10 @@ def test_context_parallel_steps_on_one_gpu(gdn):
     outs[0], s = ops.prefill(*(locs[0][x] for x in keys), dev["state"], *gate(locs[0]), dev["scale"])
     affine = [None] + [ops.affine(*(locs[r][x] for x in keys), *gate(locs[r]), dev["scale"])
                        for r in range(1, world)]
-    pairs = [(torch.zeros_like(s), s)] + [(affine[r][1], affine[r][2]) for r in range(1, world)]
+    pairs = torch.stack([torch.stack([torch.zeros_like(s), s])] +
+                        [torch.stack([affine[r][1], affine[r][2]]) for r in range(1, world)])
     for r in range(1, world):
-        s_in = torch.zeros_like(s)
-        for j in range(r):
-            s_in = ops.compose(s_in, *pairs[j])
-        outs[r], s_r = ops.finish(affine[r][0], s_in)
+        outs[r], s_r = ops.finish(affine[r][0], pairs[:r])  # folds the preceding ranges' maps on the GPU
     torch.cuda.synchronize()
     o_ref, s_ref = oracle_prefill(inp)
     o_ref = ref.bf16_bits_to_f32(o_ref)
