@@ -168,3 +168,44 @@ def test_decode_pooled_rejects_bad_arguments(lib):
     assert call(D=64) == 2
     assert call(flags=0x2) == 1
     assert call(B=0) == 0 and call(T=0) == 0
+
+
+def test_range_workspace_size(lib):
+    """gdn_prefill_range_affine / _finish (GDN_FLAG_RANGE_AFFINE): records, then [3][N][S - 1][HV]
+    64 KB states (every segment of the range is a map pair: S - 1 of them), then the homogeneous
+    outputs [T][HV][128] bf16.  Automatic pair count (148 SMs assumed without a GPU): one
+    16,384-token range of 32 v-heads gets 2 (128 CTAs of half a range in one wave); forced with
+    GDN_PREFILL_SEGMENTS(n)."""
+    ra, seg = 0x8, (lambda n: (n & 15) << 8)  # noqa: E731
+    st = 128 * 128 * 4
+    rec = (16384 // 64 + 1 + 1) * 32 * 11008
+    phi = 16384 * 32 * 256
+    assert lib.gdn_prefill_workspace_size(1, 16384, 16, 32, 128, ra) == rec + 3 * 2 * 32 * st + phi
+    assert lib.gdn_prefill_workspace_size(1, 16384, 16, 32, 128, ra | seg(1)) == rec + 3 * 1 * 32 * st + phi
+    assert lib.gdn_prefill_workspace_size(1, 16384, 16, 32, 128, ra | seg(4)) == rec + 3 * 4 * 32 * st + phi
+
+
+def test_range_calls_reject_bad_arguments(lib):
+    def affine(**over):
+        a = dict(ws=None, wsb=0, flags=0x8, mm=16, out=16)
+        a.update(over)
+        return lib.gdn_prefill_range_affine(16, 2048, 128, 16, 2048, 128, 16, 4096, 128, 16, 8, 32, 16, 8, 32,
+                                            8, 0, 0.0, a["out"], 4096, 128, a["mm"], 32 * 16384, 16384,
+                                            16, 32 * 16384, 16384, 1, 640, 16, 32, 128, a["ws"], a["wsb"],
+                                            a["flags"], None)
+    assert affine(flags=0x8 | 0x1) == 1 and "flag" in lib.gdn_last_error().decode()  # no q/k L2 norm here
+    assert affine(mm=None) == 1
+    assert affine(out=24) == 2  # not 16-byte aligned
+    assert affine() == 4 and "workspace" in lib.gdn_last_error().decode()
+
+    def finish(**over):
+        a = dict(state=None, prev=None, nprev=0, ns=16, ws=None, wsb=0)
+        a.update(over)
+        return lib.gdn_prefill_range_finish(8, 0, a["state"], 32 * 16384, 16384, a["prev"], a["nprev"],
+                                            16, 4096, 128, a["ns"], 32 * 16384, 16384, 1, 640, 16, 32, 128,
+                                            a["ws"], a["wsb"], 0x8, None)
+    assert finish(state=16, prev=16, nprev=2) == 1 and "not both" in lib.gdn_last_error().decode()
+    assert finish(nprev=-1) == 1
+    assert finish(prev=None, nprev=1) == 1
+    assert finish(ns=None) == 1
+    assert finish() == 4
