@@ -23,8 +23,9 @@ the run from the identity).  So:
 
 Both rank 0's prefill and the other ranks' affine pass cut their ranges into segments on
 separate SMs; measured on one long 32-head sequence, rank 0's prefill of a range takes
-about as long as an affine pass of an equal one, so ``FIRST_RANK_WEIGHT`` is 1.  The reference has no long-context
-parallelism (its prefill is token-serial per sequence, ``solution/triton/kernel_prefill.py:88``).
+about as long as an affine pass of an equal one, so ``FIRST_RANK_WEIGHT`` is 1.  The
+reference has no long-context parallelism (its prefill is token-serial per sequence,
+``solution/triton/kernel_prefill.py:88``).
 
 ``split_ranges``/``local_inputs`` cut a global varlen batch into rank-local inputs:
 every range of a sequence starts on a 64-token chunk boundary.
